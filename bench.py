@@ -1,0 +1,821 @@
+"""Benchmark of the bo-kernel-tuner hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload rmsnorm|gemm8192|gemm2048|moe_small|moe_large]
+
+Prints ONE JSON line (rank 0).  A step is one pass of the workload's hot path
+over one batch of synthetic input already resident in HBM; K steps are
+captured in CUDA graphs and replayed between a barrier + synchronize on both
+sides, timed with CUDA events on the launching stream, max over ranks.
+
+Workloads (default ``rmsnorm``, the 4096 x 4096 bf16 RMSNorm):
+  rmsnorm    x[4096,4096] bf16 per rank (rows of a G*4096-row matrix split
+             across G ranks, no collective: weak scaling); GB/s.
+  gemm8192   C = A.B bf16 8192^3; B and C split along N across ranks (A
+             replicated, no collective: strong scaling); TFLOP/s.
+  gemm2048   2048^3 bf16, replicas; TFLOP/s.
+  moe_small  8-expert grouped GEMM, 1528 tokens, replicas; TFLOP/s.
+  moe_large  64 experts x [4096, 14336], 16384 tokens top-2 Zipf(1.1),
+             one GPU: device routing + gather + grouped GEMM; TFLOP/s.
+
+Inputs larger than L2 (126 MB) or rotated through buffer sets that together
+exceed it, so every step reads from HBM.  ``--impl reference`` times the
+reference's FP32 CPU path (the oracle port, numpy) on the host cores.
+"""
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "TFLOP/s (GEMM, MoE grouped GEMM) & RMSNorm GB/s vs B200 peak at 1–8 GPUs"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+L2_BYTES = 126 * 1024 * 1024
+
+
+# ----------------------------------------------------------------------------- utilities
+def load_peaks():
+    path = REPO / "MEASURED_PEAKS.json"
+    if path.exists():
+        try:
+            data = json.loads(path.read_text())
+            return data, "measured"
+        except ValueError:
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def profile_traffic(workload):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
+    path = REPO / "profiles" / "traffic.json"
+    if not path.exists():
+        return None
+    try:
+        return json.loads(path.read_text()).get(workload)
+    except ValueError:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu), "-lms", "50"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.perf_counter(), line.strip()))
+
+    def stop(self, t0, t1):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.12)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        window = [line for t, line in self.lines if t0 - 0.15 <= t <= t1 + 0.15] or \
+                 [line for _, line in self.lines]
+        sm, smax, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in window:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": max(smax) if smax else None,
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+        }
+
+
+def kernel_durations_ms(stream, launches):
+    """Device duration of each launch in ``launches`` (callables issuing one
+    kernel each), measured with CUDA events on ``stream``.  A sleep kernel
+    queued first keeps the GPU busy while the host enqueues, so each event
+    pair brackets only its kernel."""
+    import torch
+
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in launches]
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(int(2e6) + 200000 * len(launches))
+        for (begin, end), fn in zip(events, launches):
+            begin.record(stream)
+            fn()
+            end.record(stream)
+    stream.synchronize()
+    return [b.elapsed_time(e) for b, e in events]
+
+
+def cpu_threads():
+    return os.cpu_count() or 1
+
+
+# ----------------------------------------------------------------------------- workloads
+class Rmsnorm:
+    name = "rmsnorm"
+    unit = "GB/s"
+    dtype = "bf16"
+    kernel = "rmsnorm_vec_kernel<bf16,4>"
+    bound = "hbm"
+
+    def __init__(self, device, rank, world):
+        import torch
+
+        from flashattentionanycard_b200 import workloads
+        from flashattentionanycard_b200.configs.search_spaces import default_params
+
+        cfg = workloads.RMSNORM
+        self.m, self.n, self.eps = cfg["m"], cfg["n"], cfg["eps"]
+        self.params = default_params("rmsnorm")
+        self.bytes_per_step = 2 * self.m * self.n * 2 + self.n * 2  # x in + y out + w
+        # Rank r owns rows [r*m, (r+1)*m) of a (world*m)-row matrix: distinct seed per shard.
+        x, w = workloads.rmsnorm_inputs(self.m, self.n, "bf16", seed=rank, device=device)
+        per_set = 2 * x.numel() * 2
+        self.sets = max(2, math.ceil(2 * L2_BYTES / per_set))
+        self.x = [x] + [x.roll(i, 0).contiguous() for i in range(1, self.sets)]
+        self.y = [torch.empty_like(x) for _ in range(self.sets)]
+        self.w = w
+        self.units = f"{self.m}x{self.n} rows x hidden per rank"
+
+    def step(self, i):
+        from flashattentionanycard_b200.kernels import rmsnorm
+
+        s = i % self.sets
+        rmsnorm.launch(self.x[s], self.w, self.y[s], self.params, self.eps)
+
+    launches_per_step = 1
+
+    def config(self, world):
+        return {"workload": f"rmsnorm_bf16_{self.m}x{self.n}_eps1e-6",
+                "rows_per_gpu": self.m, "hidden": self.n, "total_rows": self.m * world,
+                "partition": "row-split, no collective", "l2": f"rotating {self.sets} buffer sets "
+                f"({self.sets * 2 * self.m * self.n * 2 / 2**20:.0f} MiB > L2)",
+                "params": self.params}
+
+    def value(self, seconds_per_step, world):
+        return self.bytes_per_step * world / seconds_per_step / 1e9
+
+    # e2e through the public API with host buffers
+    def e2e_setup(self):
+        import torch
+
+        self.hx = self.x[0].cpu().pin_memory()
+        self.hw = self.w.cpu().pin_memory()
+        self.hy = torch.empty_like(self.hx).pin_memory()
+        self.dx = torch.empty_like(self.x[0])
+        self.dw = torch.empty_like(self.w)
+        self.dy = torch.empty_like(self.x[0])
+        self.h2d = self.hx.numel() * 2 + self.hw.numel() * 2
+        self.d2h = self.hy.numel() * 2
+
+    def e2e_step(self):
+        from flashattentionanycard_b200.kernels import rmsnorm
+
+        self.dx.copy_(self.hx, non_blocking=True)
+        self.dw.copy_(self.hw, non_blocking=True)
+        rmsnorm.launch(self.dx, self.dw, self.dy, self.params, self.eps)
+        self.hy.copy_(self.dy, non_blocking=True)
+
+    # CPU reference (oracle port): fp32 RMSNorm over row blocks on all host threads
+    def cpu_setup(self):
+        import numpy as np
+
+        from flashattentionanycard_b200 import workloads
+
+        x, w = workloads.rmsnorm_inputs(self.m, self.n, "bf16", seed=0)
+        self.cx = x.float().numpy()
+        self.cw = w.float().numpy()
+        self.cout = np.empty_like(self.cx)
+
+    def cpu_step(self, pool, threads):
+        from oracle import numerics
+
+        rows = self.m
+        chunk = max(1, -(-rows // threads))
+
+        def work(lo):
+            hi = min(rows, lo + chunk)
+            self.cout[lo:hi] = numerics.rmsnorm_fp32(self.cx[lo:hi], self.cw, self.eps)
+
+        list(pool.map(work, range(0, rows, chunk)))
+        return self.bytes_per_step
+
+
+class Gemm:
+    unit = "TFLOP/s"
+    bound = "tensor"
+    launches_per_step = 1
+
+    def __init__(self, device, rank, world, size, dtype="bf16", split=True):
+        import torch
+
+        from flashattentionanycard_b200 import workloads
+        from flashattentionanycard_b200.configs.search_spaces import default_params
+
+        self.name = f"gemm{size}"
+        self.dtype = dtype
+        self.size = size
+        self.kernel = "gemm_tc_kernel<256,dense>"
+        self.params = default_params("gemm")
+        n_local = size // world if split else size
+        if split and size % world:
+            raise SystemExit("N must divide evenly across ranks")
+        a, b = workloads.gemm_inputs(size, size, size, dtype, seed=0, device=device)
+        if split:
+            b = b[:, rank * n_local:(rank + 1) * n_local].contiguous()
+        self.a, self.b = a, b
+        self.n_local = n_local
+        self.flops_per_step = 2.0 * size * size * n_local
+        per_set = (a.numel() + b.numel() + size * n_local) * 2
+        self.sets = max(1, math.ceil(2 * L2_BYTES / per_set)) if per_set < 2 * L2_BYTES else 1
+        self.A = [a] + [a.roll(i, 0).contiguous() for i in range(1, self.sets)]
+        self.C = [torch.empty(size, n_local, device=device, dtype=a.dtype) for _ in range(self.sets)]
+        self.split = split
+
+    def step(self, i):
+        from flashattentionanycard_b200.kernels import gemm
+
+        s = i % self.sets
+        gemm.launch(self.A[s], self.b, self.C[s], self.params)
+
+    def config(self, world):
+        return {"workload": f"gemm_{self.dtype}_{self.size}^3", "m": self.size, "k": self.size,
+                "n": self.size, "n_per_gpu": self.n_local,
+                "partition": "N-split, A replicated, no collective" if self.split else "replicas",
+                "l2": "inputs > L2" if self.sets == 1 else f"rotating {self.sets} A/C sets",
+                "params": self.params}
+
+    def value(self, seconds_per_step, world):
+        total = self.flops_per_step * (world if not self.split else world)
+        return total / seconds_per_step / 1e12
+
+    def e2e_setup(self):
+        import torch
+
+        self.ha = self.a.cpu().pin_memory()
+        self.hb = self.b.cpu().pin_memory()
+        self.hc = torch.empty(self.size, self.n_local, dtype=self.a.dtype).pin_memory()
+        self.da, self.db = torch.empty_like(self.a), torch.empty_like(self.b)
+        self.dc = torch.empty(self.size, self.n_local, device=self.a.device, dtype=self.a.dtype)
+        self.h2d = (self.ha.numel() + self.hb.numel()) * 2
+        self.d2h = self.hc.numel() * 2
+
+    def e2e_step(self):
+        from flashattentionanycard_b200.kernels import gemm
+
+        self.da.copy_(self.ha, non_blocking=True)
+        self.db.copy_(self.hb, non_blocking=True)
+        gemm.launch(self.da, self.db, self.dc, self.params)
+        self.hc.copy_(self.dc, non_blocking=True)
+
+    def cpu_setup(self):
+        from flashattentionanycard_b200 import workloads
+
+        rows = 256 if self.size > 2048 else self.size
+        a, b = workloads.gemm_inputs(self.size, self.size, self.size, self.dtype, seed=0)
+        self.ca = a[:rows].float().numpy()
+        self.cb = b[:, : self.n_local].float().numpy()
+        self.cpu_rows = rows
+
+    def cpu_step(self, pool, threads):
+        from oracle import numerics
+
+        numerics.gemm_fp32(self.ca, self.cb)  # BLAS threads
+        return 2.0 * self.cpu_rows * self.size * self.n_local
+
+
+class MoeSmall:
+    name = "moe_small"
+    unit = "TFLOP/s"
+    bound = "hbm"
+    dtype = "bf16"
+    kernel = "gemm_tc_kernel<256,grouped>"
+    launches_per_step = 1
+
+    def __init__(self, device, rank, world):
+        import torch
+
+        from flashattentionanycard_b200 import workloads
+        from flashattentionanycard_b200.configs.search_spaces import default_params
+
+        counts = workloads.MOE_SMALL_COUNTS
+        cfg = workloads.MOE_SMALL
+        self.k, self.n = cfg["k"], cfg["n"]
+        self.params = default_params("moe_grouped_gemm")
+        x, w = workloads.moe_inputs(counts, self.k, self.n, "bf16", seed=rank, device=device)
+        self.offsets = torch.tensor(workloads.offsets_from_counts(counts), dtype=torch.int32,
+                                    device=device)
+        t = x.shape[0]
+        self.flops_per_step = 2.0 * t * self.k * self.n
+        nonempty = sum(1 for c in counts if c)
+        self.bytes_per_step = (t * self.k + nonempty * self.k * self.n + t * self.n) * 2
+        per_set = self.bytes_per_step
+        self.sets = max(2, math.ceil(2 * L2_BYTES / per_set))
+        self.X = [x] + [x.roll(i, 0).contiguous() for i in range(1, self.sets)]
+        self.W = [w] + [w.roll(i, 1).contiguous() for i in range(1, self.sets)]
+        self.Y = [torch.empty(t, self.n, device=device, dtype=x.dtype) for _ in range(self.sets)]
+        self.counts = counts
+        self.sm = torch.cuda.get_device_properties(device).multi_processor_count
+
+    def step(self, i):
+        from flashattentionanycard_b200.kernels import moe_grouped_gemm
+
+        s = i % self.sets
+        moe_grouped_gemm.launch(self.X[s], self.W[s], self.offsets, self.Y[s], self.params, self.sm)
+
+    def config(self, world):
+        return {"workload": "moe_grouped_gemm_bf16_E8_K1024_N2048_T1528",
+                "expert_tokens": list(self.counts), "partition": "replicas",
+                "l2": f"rotating {self.sets} X/W/Y sets", "params": self.params}
+
+    def value(self, seconds_per_step, world):
+        return self.flops_per_step * world / seconds_per_step / 1e12
+
+    def e2e_setup(self):
+        import torch
+
+        self.hx, self.hwt = self.X[0].cpu().pin_memory(), self.W[0].cpu().pin_memory()
+        self.hy = torch.empty(self.Y[0].shape, dtype=self.Y[0].dtype).pin_memory()
+        self.dx, self.dw = torch.empty_like(self.X[0]), torch.empty_like(self.W[0])
+        self.dy = torch.empty_like(self.Y[0])
+        self.h2d = (self.hx.numel() + self.hwt.numel()) * 2
+        self.d2h = self.hy.numel() * 2
+
+    def e2e_step(self):
+        from flashattentionanycard_b200.kernels import moe_grouped_gemm
+
+        self.dx.copy_(self.hx, non_blocking=True)
+        self.dw.copy_(self.hwt, non_blocking=True)
+        moe_grouped_gemm.launch(self.dx, self.dw, self.offsets, self.dy, self.params, self.sm)
+        self.hy.copy_(self.dy, non_blocking=True)
+
+    def cpu_setup(self):
+        from flashattentionanycard_b200 import workloads
+
+        x, w = workloads.moe_inputs(self.counts, self.k, self.n, "bf16", seed=0)
+        self.cx, self.cw = x.float().numpy(), w.float().numpy()
+        self.cstarts = workloads.offsets_from_counts(self.counts)
+
+    def cpu_step(self, pool, threads):
+        from oracle import numerics
+
+        numerics.grouped_gemm_fp32(self.cx, self.cw, self.cstarts)
+        return self.flops_per_step
+
+
+class MoeLarge:
+    name = "moe_large"
+    unit = "TFLOP/s"
+    bound = "tensor"
+    dtype = "bf16"
+    kernel = "gemm_tc_kernel<256,grouped>"
+    launches_per_step = 5  # route: count, scan, scatter; gather; grouped GEMM
+
+    def __init__(self, device, rank, world):
+        import torch
+
+        from flashattentionanycard_b200 import workloads
+        from flashattentionanycard_b200.configs.search_spaces import default_params
+        from flashattentionanycard_b200.kernels.moe_routing import MoeRouter
+
+        if world > 1:
+            raise SystemExit("moe_large runs on one GPU in this build (expert parallelism pending)")
+        cfg = workloads.MOE_LARGE
+        self.cfg = cfg
+        self.params = default_params("moe_grouped_gemm")
+        self.x, self.w, ids = workloads.moe_large_inputs("bf16", seed=0, device=device)
+        self.ids = ids.reshape(-1).to(device)
+        a = self.ids.numel()
+        self.router = MoeRouter(a, cfg["experts"], device)
+        self.packed = torch.empty(a, cfg["k"], device=device, dtype=torch.bfloat16)
+        self.y = torch.empty(a, cfg["n"], device=device, dtype=torch.bfloat16)
+        self.flops_per_step = 2.0 * a * cfg["k"] * cfg["n"]
+        self.sm = torch.cuda.get_device_properties(device).multi_processor_count
+
+    def step(self, i):
+        from flashattentionanycard_b200.kernels import moe_grouped_gemm
+        from flashattentionanycard_b200.kernels.moe_routing import gather_rows
+
+        self.router(self.ids)
+        gather_rows(self.x, self.router.perm, self.packed, divisor=self.cfg["topk"])
+        moe_grouped_gemm.launch(self.packed, self.w, self.router.offsets, self.y, self.params,
+                                self.sm)
+
+    def config(self, world):
+        c = self.cfg
+        return {"workload": f"moe_bf16_E{c['experts']}_K{c['k']}_N{c['n']}_T{c['tokens']}_top2_zipf1.1",
+                "partition": "single GPU (all experts local)",
+                "step": "route + gather + grouped GEMM", "l2": "W 7.5 GB > L2",
+                "params": self.params}
+
+    def value(self, seconds_per_step, world):
+        return self.flops_per_step * world / seconds_per_step / 1e12
+
+    def e2e_setup(self):
+        import torch
+
+        self.hx = self.x.cpu().pin_memory()
+        self.hids = self.ids.cpu().pin_memory()
+        self.hy = torch.empty(self.y.shape, dtype=self.y.dtype).pin_memory()
+        self.dx, self.dids = torch.empty_like(self.x), torch.empty_like(self.ids)
+        self.h2d = self.hx.numel() * 2 + self.hids.numel() * 4
+        self.d2h = self.hy.numel() * 2
+
+    def e2e_step(self):
+        from flashattentionanycard_b200.kernels import moe_grouped_gemm
+        from flashattentionanycard_b200.kernels.moe_routing import gather_rows
+
+        self.dx.copy_(self.hx, non_blocking=True)
+        self.dids.copy_(self.hids, non_blocking=True)
+        self.router(self.dids)
+        gather_rows(self.dx, self.router.perm, self.packed, divisor=self.cfg["topk"])
+        moe_grouped_gemm.launch(self.packed, self.w, self.router.offsets, self.y, self.params,
+                                self.sm)
+        self.hy.copy_(self.y, non_blocking=True)
+
+    def cpu_setup(self):
+        import numpy as np
+
+        c = self.cfg
+        self.cx = self.x[:256].float().cpu().numpy()
+        self.cw = self.w[0].float().cpu().numpy()
+        self.cpu_flops = 2.0 * 256 * c["k"] * c["n"]
+        self._np = np
+
+    def cpu_step(self, pool, threads):
+        from oracle import numerics
+
+        numerics.gemm_fp32(self.cx, self.cw)
+        return self.cpu_flops
+
+
+WORKLOADS = {
+    "rmsnorm": lambda d, r, w: Rmsnorm(d, r, w),
+    "gemm8192": lambda d, r, w: Gemm(d, r, w, 8192, "bf16", split=True),
+    "gemm2048": lambda d, r, w: Gemm(d, r, w, 2048, "bf16", split=False),
+    "moe_small": lambda d, r, w: MoeSmall(d, r, w),
+    "moe_large": lambda d, r, w: MoeLarge(d, r, w),
+}
+DEFAULT_STEPS = {"rmsnorm": 4000, "gemm8192": 200, "gemm2048": 2000, "moe_small": 4000,
+                 "moe_large": 100}
+
+
+# ----------------------------------------------------------------------------- CPU reference
+def cpu_measure(workload, seconds, min_reps=3):
+    """Time the oracle port of the workload on the host cores for ~``seconds``."""
+    import numpy as np
+
+    threads = cpu_threads()
+    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    workload.cpu_setup()
+    with ThreadPoolExecutor(threads) as pool:
+        workload.cpu_step(pool, threads)  # warm
+        reps, work, t0 = 0, 0.0, time.perf_counter()
+        while reps < min_reps or time.perf_counter() - t0 < seconds:
+            work += workload.cpu_step(pool, threads)
+            reps += 1
+        elapsed = time.perf_counter() - t0
+    del np
+    scale = 1e9 if workload.unit == "GB/s" else 1e12
+    return work / elapsed / scale, reps, elapsed, threads
+
+
+def cpu_sample_description(workload):
+    if workload.name == "rmsnorm":
+        return "numpy fp32 RMSNorm of the full 4096x4096 input, rows split over host threads"
+    if workload.name.startswith("gemm"):
+        return (f"numpy/BLAS fp32 GEMM of {workload.cpu_rows} rows of A x B[:, :{workload.n_local}]"
+                f" (K={workload.size})")
+    if workload.name == "moe_small":
+        return "numpy/BLAS fp32 per-expert GEMMs of the full 8-expert problem"
+    return "numpy/BLAS fp32 GEMM of 256 tokens x one expert's W[4096, 14336]"
+
+
+def run_reference(args):
+    """--impl reference: the reference's FP32 CPU path (oracle port) on the host."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import torch
+
+    torch.set_num_threads(cpu_threads())
+    wl = WORKLOADS[args.workload]
+    device = "cpu"
+    # Build the workload description without a GPU: only the CPU legs are used.
+    workload = _cpu_only_workload(args.workload)
+    times = []
+    work = 0.0
+    threads = cpu_threads()
+    workload.cpu_setup()
+    with ThreadPoolExecutor(threads) as pool:
+        for _ in range(args.warmup):
+            workload.cpu_step(pool, threads)
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            work += workload.cpu_step(pool, threads)
+            times.append(time.perf_counter() - t0)
+    total = sum(times)
+    scale = 1e9 if workload.unit == "GB/s" else 1e12
+    value = work / total / scale
+    del wl, device
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": workload.unit,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload.cpu_config(),
+        "cpu_baseline": {"value": value, "unit": workload.unit, "cores": threads,
+                         "kind": "port", "sample": cpu_sample_description(workload)},
+        "e2e": {"value": value, "unit": workload.unit, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def _cpu_only_workload(name):
+    """A workload object whose CPU legs run without touching a GPU."""
+    from flashattentionanycard_b200 import workloads
+
+    class CpuOnly:
+        pass
+
+    if name == "rmsnorm":
+        w = Rmsnorm.__new__(Rmsnorm)
+        cfg = workloads.RMSNORM
+        w.m, w.n, w.eps = cfg["m"], cfg["n"], cfg["eps"]
+        w.bytes_per_step = 2 * w.m * w.n * 2 + w.n * 2
+        w.cpu_config = lambda: {"workload": f"rmsnorm_bf16_{w.m}x{w.n}_eps1e-6",
+                                "sample": "full 4096x4096 per step"}
+        return w
+    if name in ("gemm8192", "gemm2048"):
+        w = Gemm.__new__(Gemm)
+        w.size = 8192 if name == "gemm8192" else 2048
+        w.name, w.dtype, w.n_local = name, "bf16", w.size
+        w.cpu_config = lambda: {"workload": f"gemm_bf16_{w.size}^3",
+                                "sample": f"{256 if w.size > 2048 else w.size} rows of A per step"}
+        return w
+    if name == "moe_small":
+        w = MoeSmall.__new__(MoeSmall)
+        w.counts = workloads.MOE_SMALL_COUNTS
+        w.k, w.n = workloads.MOE_SMALL["k"], workloads.MOE_SMALL["n"]
+        w.flops_per_step = 2.0 * sum(w.counts) * w.k * w.n
+        w.cpu_config = lambda: {"workload": "moe_grouped_gemm_bf16_E8_K1024_N2048_T1528"}
+        return w
+    w = CpuOnly()
+    cfg = workloads.MOE_LARGE
+    w.name, w.unit = "moe_large", "TFLOP/s"
+
+    def setup():
+        import torch
+
+        g = torch.Generator().manual_seed(0)
+        w.cx = torch.randn(256, cfg["k"], generator=g).bfloat16().float().numpy()
+        w.cw = (0.02 * torch.randn(cfg["k"], cfg["n"], generator=g)).bfloat16().float().numpy()
+
+    def step(pool, threads):
+        from oracle import numerics
+
+        numerics.gemm_fp32(w.cx, w.cw)
+        return 2.0 * 256 * cfg["k"] * cfg["n"]
+
+    w.cpu_setup, w.cpu_step = setup, step
+    w.cpu_config = lambda: {"workload": "moe_bf16_E64_K4096_N14336_T16384_top2_zipf1.1",
+                            "sample": "256 tokens x one expert per step"}
+    return w
+
+
+# ----------------------------------------------------------------------------- GPU arm
+def capture_steps(workload, stream, first, count):
+    import torch
+
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(first, first + count):
+            workload.step(i)
+    return graph
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        if world == 1 and args.gpus > 1:
+            raise SystemExit("--gpus N > 1 must be launched with torch.distributed.run")
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+
+    from flashattentionanycard_b200 import _native
+
+    _native.load()
+    peaks, peak_kind = load_peaks()
+    workload = WORKLOADS[args.workload](device, rank, world)
+    stream = torch.cuda.Stream(device)
+    torch.cuda.synchronize()
+
+    # warm-up (eager, outside capture: first calls set kernel attributes)
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            workload.step(i)
+    stream.synchronize()
+    _native.device_status(reset=True)
+
+    steps = args.steps
+    chunk = max(1, min(steps, 250))
+    graphs = []
+    done = 0
+    while done < steps:
+        count = min(chunk, steps - done)
+        graphs.append(capture_steps(workload, stream, done, count))
+        done += count
+    # one untimed replay of the first graph (graph upload)
+    graphs[0].replay()
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    begin, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    begin.record(stream)
+    with torch.cuda.stream(stream):
+        for g in graphs:
+            g.replay()
+    end.record(stream)
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop(t0, t1)
+    ms = begin.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    code, detail = _native.device_status(reset=True)
+    if code:
+        raise SystemExit(f"kernel reported device status {code} (detail {detail})")
+    del graphs
+    ms_per_step = ms / steps
+    value = workload.value(ms_per_step / 1e3, world)
+
+    # dominant kernel: per-launch device duration with CUDA events on its stream
+    if workload.launches_per_step == 1:
+        launches = [(lambda i=i: workload.step(i)) for i in range(min(steps, 50))]
+    else:
+        launches = [(lambda i=i: _last_kernel(workload, i)) for i in range(20)]
+        for i in range(3):
+            with torch.cuda.stream(stream):
+                workload.step(i)
+        stream.synchronize()
+    durations = kernel_durations_ms(stream, launches)
+    kernel_ms = statistics.median(durations)
+    if workload.bound == "hbm" and workload.unit == "GB/s":
+        achieved = workload.bytes_per_step / (kernel_ms / 1e3) / 1e9
+        peak = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+        unit_r = "GB/s"
+    elif workload.bound == "hbm":
+        achieved = workload.bytes_per_step / (kernel_ms / 1e3) / 1e9
+        peak = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+        unit_r = "GB/s"
+    else:
+        achieved = workload.flops_per_step / (kernel_ms / 1e3) / 1e12
+        peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+        unit_r = "TFLOP/s"
+    roofline = {"kernel": workload.kernel, "bound": "hbm" if unit_r == "GB/s" else "tensor",
+                "achieved": achieved, "peak": peak, "unit": unit_r, "frac": achieved / peak,
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json)" if peak_kind == "measured"
+                else "fallback", "kernel_ms_median": kernel_ms,
+                "traffic": profile_traffic(workload.name)}
+
+    # end to end through the public API with pinned host buffers
+    workload.e2e_setup()
+    e2e_steps = max(3, min(20, steps))
+    with torch.cuda.stream(stream):
+        workload.e2e_step()
+    stream.synchronize()
+    if world > 1:
+        dist.barrier()
+    eb, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    eb.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(e2e_steps):
+            workload.e2e_step()
+    ee.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = eb.elapsed_time(ee) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e = {"value": workload.value(e2e_ms / 1e3, world), "unit": workload.unit,
+           "h2d_bytes_per_step": workload.h2d, "d2h_bytes_per_step": workload.d2h,
+           "ms_per_step": e2e_ms, "steps": e2e_steps,
+           "api": "flashattentionanycard_b200.kernels launch() with pinned host copies"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, reps, elapsed, threads = cpu_measure(_cpu_only_workload(args.workload),
+                                                args.cpu_seconds)
+        cpu = {"value": v, "unit": workload.unit, "cores": threads, "kind": "port",
+               "sample": cpu_sample_description(_cpu_only_workload(args.workload)) +
+               f"; {reps} reps in {elapsed:.1f} s"}
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    scaling = "weak" if args.workload in ("rmsnorm", "gemm2048", "moe_small") else "strong"
+    line = {
+        "metric": METRIC, "value": value, "unit": workload.unit, "n_gpus": world,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
+        "dtype": workload.dtype, "data": "synthetic (seeded, BASELINE config shapes)",
+        "config": workload.config(world), "roofline": roofline, "cpu_baseline": cpu,
+        "e2e": e2e, "clocks": clocks, "gpu_launches": steps * workload.launches_per_step,
+        "impl": "ours",
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def _last_kernel(workload, i):
+    from flashattentionanycard_b200.kernels import moe_grouped_gemm
+
+    moe_grouped_gemm.launch(workload.packed, workload.w, workload.router.offsets, workload.y,
+                            workload.params, workload.sm)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="rmsnorm")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 20 if args.impl == "reference" else DEFAULT_STEPS[args.workload]
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,200 @@
+"""ctypes binding of the in-tree C-ABI library ``libbokt_sm100.so`` (include/bokt.h).
+
+The library is the only compute path: there is no Triton, PyTorch or CPU
+fallback behind the ``launch`` functions.  A missing or stale library raises
+``RuntimeError`` at the first call instead of silently running something else.
+"""
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+PACKAGE_DIR = Path(__file__).resolve().parent
+LIBRARY_PATH = PACKAGE_DIR / "libbokt_sm100.so"
+ABI_VERSION = 1
+
+FP16, BF16 = 0, 1
+KERNEL_GEMM, KERNEL_RMSNORM, KERNEL_MOE_GROUPED_GEMM = 0, 1, 2
+
+ERRORS = {
+    1: "invalid argument",
+    2: "unsupported",
+    3: "invalid launch configuration",
+    4: "CUDA error",
+    5: "device-reported failure",
+}
+
+# Public parameter names (search-space keys) -> bokt_params fields.
+PARAM_FIELDS = {
+    "BLOCK_M": "block_m",
+    "BLOCK_N": "block_n",
+    "BLOCK_K": "block_k",
+    "num_stages": "stages",
+    "GROUP_M": "group_m",
+    "CTA_MULTIPLIER": "cta_multiplier",
+    "num_warps": "num_warps",
+    "ROWS_PER_CTA": "rows_per_cta",
+    "SPLIT_K": "split_k",
+    "CTA_GROUP": "cta_group",
+}
+
+
+class BoktParams(ctypes.Structure):
+    _fields_ = [
+        ("block_m", ctypes.c_int32),
+        ("block_n", ctypes.c_int32),
+        ("block_k", ctypes.c_int32),
+        ("stages", ctypes.c_int32),
+        ("group_m", ctypes.c_int32),
+        ("cta_multiplier", ctypes.c_int32),
+        ("num_warps", ctypes.c_int32),
+        ("rows_per_cta", ctypes.c_int32),
+        ("split_k", ctypes.c_int32),
+        ("cta_group", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 6),
+    ]
+
+
+class BoktAttrs(ctypes.Structure):
+    _fields_ = [
+        ("shared_bytes", ctypes.c_int32),
+        ("registers", ctypes.c_int32),
+        ("local_bytes", ctypes.c_int32),
+        ("threads", ctypes.c_int32),
+        ("max_threads", ctypes.c_int32),
+        ("path", ctypes.c_int32),
+    ]
+
+
+_VP, _I32, _I64, _F32 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float
+_PP = ctypes.POINTER(BoktParams)
+
+SIGNATURES = {
+    "bokt_abi_version": (_I32, []),
+    "bokt_built_sm": (_I32, []),
+    "bokt_last_error": (ctypes.c_char_p, []),
+    "bokt_gemm": (_I32, [_VP, _VP, _VP, _I32, _I32, _I32, _I32, _PP, _VP]),
+    "bokt_rmsnorm": (_I32, [_VP, _VP, _VP, _I32, _I32, _F32, _I32, _PP, _VP]),
+    "bokt_moe_grouped_gemm": (
+        _I32,
+        [_VP, _VP, _VP, _I32, _VP, _I32, _I32, _I32, _I32, _I32, _I32, _PP, _VP],
+    ),
+    "bokt_moe_route_workspace_bytes": (_I64, [_I32, _I32]),
+    "bokt_moe_route": (_I32, [_VP, _I32, _I32, _VP, _VP, _VP, _VP, _VP, _VP, _I64, _VP]),
+    "bokt_gather_rows": (_I32, [_VP, _I64, _VP, _VP, _I32, _I32, _I32, _I32, _VP]),
+    "bokt_kernel_attrs": (
+        _I32,
+        [_I32, _I32, _I32, _I32, _PP, ctypes.POINTER(BoktAttrs)],
+    ),
+    "bokt_device_status": (
+        _I32,
+        [ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int), _I32],
+    ),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+def load():
+    """Load (once) and return the ctypes library; raise RuntimeError if absent."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = Path(os.environ.get("BOKT_LIBRARY", LIBRARY_PATH))
+        if not path.exists():
+            raise RuntimeError(
+                f"sm_100a kernel library not built: {path} is missing "
+                "(run `make -C flashattentionanycard_b200/csrc` or __graft_entry__.build())"
+            )
+        lib = ctypes.CDLL(str(path))
+        for name, (restype, argtypes) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = restype
+            fn.argtypes = argtypes
+        if lib.bokt_abi_version() != ABI_VERSION:
+            raise RuntimeError(f"{path}: ABI version {lib.bokt_abi_version()} != {ABI_VERSION}")
+        _lib = lib
+        return lib
+
+
+def check(rc, what):
+    """Turn a non-zero status into RuntimeError carrying bokt_last_error()."""
+    if rc != 0:
+        message = load().bokt_last_error().decode(errors="replace")
+        raise RuntimeError(f"{what} failed ({ERRORS.get(rc, rc)}): {message}")
+
+
+def make_params(params):
+    """Convert a search-space parameter dict to bokt_params (unknown keys rejected)."""
+    p = BoktParams()
+    for key, value in (params or {}).items():
+        field = PARAM_FIELDS.get(key)
+        if field is None:
+            raise ValueError(f"Unknown launch parameter {key!r}")
+        if type(value) is not int:
+            raise ValueError(f"Launch parameter {key} must be int, got {type(value).__name__}")
+        setattr(p, field, value)
+    return p
+
+
+def dtype_code(dtype):
+    import torch
+
+    if dtype == torch.bfloat16:
+        return BF16
+    if dtype == torch.float16:
+        return FP16
+    raise ValueError(f"Unsupported dtype {dtype}; expected float16 or bfloat16")
+
+
+def current_stream(device):
+    import torch
+
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def device_status(reset=True):
+    """Return (code, detail) of the device status word (synchronises the device)."""
+    lib = load()
+    code, detail = ctypes.c_int(0), ctypes.c_int(0)
+    check(lib.bokt_device_status(ctypes.byref(code), ctypes.byref(detail), 1 if reset else 0),
+          "bokt_device_status")
+    return code.value, detail.value
+
+
+class _Metadata:
+    def __init__(self, shared):
+        self.shared = shared
+
+
+class CompiledKernel:
+    """What ``launch`` returns: the fields the worker reads from Triton's
+    compiled-kernel object (tuner/worker.py:193,203-204 of the reference):
+    ``metadata.shared``, ``n_regs`` and ``n_spills``.  ``n_spills`` is the
+    kernel's local memory per thread in 4-byte words (0 when nothing spills)."""
+
+    def __init__(self, attrs):
+        self.metadata = _Metadata(int(attrs.shared_bytes))
+        self.n_regs = int(attrs.registers)
+        self.n_spills = int(attrs.local_bytes) // 4
+        self.threads = int(attrs.threads)
+        self.path = {0: "tcgen05", 1: "simt", 2: "vector", 3: "scalar"}.get(attrs.path, "?")
+
+
+_attr_cache = {}
+
+
+def kernel_attrs(kernel, dtype, n, k, params, device):
+    key = (kernel, dtype, n, k, tuple(sorted((params or {}).items())), device)
+    hit = _attr_cache.get(key)
+    if hit is None:
+        lib = load()
+        attrs = BoktAttrs()
+        p = make_params(params)
+        check(lib.bokt_kernel_attrs(kernel, dtype, n, k, ctypes.byref(p), ctypes.byref(attrs)),
+              "bokt_kernel_attrs")
+        hit = _attr_cache[key] = CompiledKernel(attrs)
+    return hit

@@ -1,0 +1,116 @@
+"""One categorical domain shared by Grid, Random and multivariate TPE, over CUDA launch parameters.
+
+Same interface as the reference's ``bo_kernel_tuner/configs/search_spaces.py``
+(``Workload`` :11-45, ``search_space`` :48-75, ``grid_size``/``grid_configs``
+:78-83, ``validate_params`` :86-89).  The domains are redefined for the sm_100a
+kernels:
+
+* GEMM / MoE grouped GEMM: ``BLOCK_M`` is the tcgen05 MMA M (128 rows, one
+  CTA); ``BLOCK_N`` the MMA N and TMEM accumulator width (x2 for double
+  buffering); ``BLOCK_K`` one 128-byte swizzle row (64 elements);
+  ``num_stages`` the depth of the TMA shared-memory ring; ``num_warps`` the
+  warp-specialised CTA (TMA + MMA + 4 epilogue warps = 6); ``GROUP_M`` the
+  grouped-M raster of the dense GEMM; ``CTA_MULTIPLIER`` the persistent grid
+  of the grouped GEMM (``sm_count * CTA_MULTIPLIER``).
+* RMSNorm: ``ROWS_PER_CTA`` and ``num_warps`` as in the reference.
+"""
+
+from dataclasses import asdict, dataclass
+from itertools import product
+from math import isfinite, prod
+
+SPACE_VERSION = 2
+KERNELS = ("gemm", "rmsnorm", "moe_grouped_gemm")
+
+
+@dataclass(frozen=True)
+class Workload:
+    kernel: str = "gemm"
+    m: int = 1024
+    n: int = 1024
+    k: int = 1024
+    dtype: str = "fp16"
+    expert_tokens: tuple[int, ...] = (64, 128, 256, 512)
+    epsilon: float = 1e-6
+    data_seed: int = 17
+
+    def __post_init__(self):
+        if self.kernel not in KERNELS or self.dtype not in ("fp16", "bf16"):
+            raise ValueError("Unknown kernel or dtype")
+        if min(self.m, self.n, self.k) <= 0 or not (isfinite(self.epsilon) and 0 < self.epsilon < 1):
+            raise ValueError("Dimensions and epsilon must be positive; epsilon < 1")
+        if not self.expert_tokens or min(self.expert_tokens) < 0 or sum(self.expert_tokens) <= 0:
+            raise ValueError("Experts require nonnegative token counts and a positive total")
+        if self.data_seed < 0:
+            raise ValueError("data_seed must be nonnegative")
+
+    def signature(self):
+        """Only semantically relevant fields enter transfer compatibility."""
+        d = asdict(self)
+        if self.kernel == "rmsnorm":
+            for key in ("k", "expert_tokens"):
+                d.pop(key)
+        else:
+            d.pop("epsilon")
+            if self.kernel == "gemm":
+                d.pop("expert_tokens")
+            else:
+                d.pop("m")
+                d["expert_tokens"] = list(self.expert_tokens)
+        return d
+
+
+def search_space(kernel: str, profile: str = "full") -> dict[str, list[int]]:
+    if kernel not in KERNELS or profile not in ("full", "smoke"):
+        raise ValueError("Unknown kernel or profile")
+    if kernel == "rmsnorm":
+        return {
+            "ROWS_PER_CTA": [1, 2, 4, 8] if profile == "full" else [1, 2],
+            "num_warps": [1, 2, 4, 8, 16] if profile == "full" else [4, 8],
+        }
+    space = {
+        "BLOCK_M": [128],
+        "BLOCK_N": [64, 128, 256],
+        "BLOCK_K": [64],
+        "num_warps": [6],
+        "num_stages": [2, 3, 4, 5, 6],
+    }
+    if profile == "smoke":
+        space = {
+            "BLOCK_M": [128],
+            "BLOCK_N": [64, 128],
+            "BLOCK_K": [64],
+            "num_warps": [6],
+            "num_stages": [2],
+        }
+    if kernel == "gemm":
+        space["GROUP_M"] = [1, 4, 8, 16] if profile == "full" else [1, 4]
+    else:
+        space["CTA_MULTIPLIER"] = [1, 2, 4] if profile == "full" else [1, 2]
+    return space
+
+
+def default_params(kernel: str) -> dict[str, int]:
+    """A good starting point on B200 (used by bench.py and as a tuning seed)."""
+    if kernel == "rmsnorm":
+        return {"ROWS_PER_CTA": 1, "num_warps": 4}
+    p = {"BLOCK_M": 128, "BLOCK_N": 256, "BLOCK_K": 64, "num_warps": 6, "num_stages": 4}
+    if kernel == "gemm":
+        p["GROUP_M"] = 8
+    else:
+        p["CTA_MULTIPLIER"] = 1
+    return p
+
+
+def grid_size(space):
+    return prod(len(v) for v in space.values())
+
+
+def grid_configs(space):
+    return (dict(zip(space, values)) for values in product(*space.values()))
+
+
+def validate_params(params, space):
+    return set(params) == set(space) and all(
+        type(params[k]) is int and params[k] in choices for k, choices in space.items()
+    )

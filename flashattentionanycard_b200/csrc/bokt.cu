@@ -1,0 +1,517 @@
+// C ABI of the sm_100a kernel library (declarations and reference citations in
+// include/bokt.h).  Host side: argument checks, path selection, TMA tensor-map
+// encoding, launch configuration.  No allocation, no synchronisation and no
+// host read-back on any compute entry point.
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/bokt.h"
+#include "bokt_device.cuh"
+#include "gemm_simt.cuh"
+#include "gemm_tc.cuh"
+#include "moe_route.cuh"
+#include "rmsnorm.cuh"
+
+namespace {
+
+thread_local char g_err[1024] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(BOKT_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int param_or(int v, int dflt) { return v > 0 ? v : dflt; }
+
+// ----------------------------------------------------------------- device info
+struct DeviceInfo {
+  int sm_count = 0;
+  int smem_optin = 0;
+};
+constexpr int kMaxDevices = 64;
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+int device_info(DeviceInfo* out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(BOKT_ERR_UNSUPPORTED, "device index %d", dev);
+  std::lock_guard<std::mutex> lock(g_dev_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (d.sm_count == 0) {
+    int major = 0;
+    e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    if (major != 10)
+      return fail(BOKT_ERR_UNSUPPORTED, "library built for sm_100a; device %d is sm_%d.x", dev,
+                  major);
+    e = cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    e = cudaDeviceGetAttribute(&d.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+  }
+  *out = d;
+  return BOKT_OK;
+}
+
+// Raise a kernel's dynamic shared-memory limit once per (device, kernel, size).
+// The first call for a configuration happens outside graph capture (warm-up).
+struct SmemAttr {
+  int dev;
+  const void* fn;
+  int bytes;
+};
+SmemAttr g_smem_attr[512];
+int g_smem_attr_n = 0;
+std::mutex g_smem_mu;
+
+int ensure_smem(const void* fn, int bytes) {
+  if (bytes <= 48 * 1024) return BOKT_OK;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(g_smem_mu);
+  for (int i = 0; i < g_smem_attr_n; ++i)
+    if (g_smem_attr[i].dev == dev && g_smem_attr[i].fn == fn && g_smem_attr[i].bytes >= bytes)
+      return BOKT_OK;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(MaxDynamicSharedMemorySize)");
+  if (g_smem_attr_n < 512) g_smem_attr[g_smem_attr_n++] = {dev, fn, bytes};
+  return BOKT_OK;
+}
+
+// ----------------------------------------------------------------- tensor maps
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+int get_encoder() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (!g_encode) return fail(BOKT_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  return BOKT_OK;
+}
+
+// Row-major [outer..., rows, cols] 16-bit tensor, box {64 cols, box_rows, 1...},
+// 128-byte swizzle, zero fill outside the tensor.
+int encode_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+               const uint64_t* strides_bytes, const uint32_t* box, bool fp16) {
+  (void)fp16;
+  int rc = get_encoder();
+  if (rc) return rc;
+  uint32_t elem_strides[3] = {1, 1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, rank, const_cast<void*>(base), dims,
+                        strides_bytes, box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(BOKT_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return BOKT_OK;
+}
+
+// ----------------------------------------------------------------- GEMM dispatch
+using bokt::GemmTcArgs;
+
+template <int BN, bool GROUPED, typename T>
+const void* tc_kernel_ptr() {
+  return reinterpret_cast<const void*>(&bokt::gemm_tc_kernel<BN, GROUPED, T>);
+}
+
+template <bool GROUPED, typename T>
+const void* tc_kernel_for(int bn) {
+  switch (bn) {
+    case 64: return tc_kernel_ptr<64, GROUPED, T>();
+    case 128: return tc_kernel_ptr<128, GROUPED, T>();
+    case 256: return tc_kernel_ptr<256, GROUPED, T>();
+  }
+  return nullptr;
+}
+
+const void* tc_kernel(bool grouped, int dtype, int bn) {
+  if (grouped)
+    return dtype == BOKT_BF16 ? tc_kernel_for<true, __nv_bfloat16>(bn)
+                              : tc_kernel_for<true, __half>(bn);
+  return dtype == BOKT_BF16 ? tc_kernel_for<false, __nv_bfloat16>(bn)
+                            : tc_kernel_for<false, __half>(bn);
+}
+
+struct TcConfig {
+  int bn, stages, group_m, smem;
+};
+
+int resolve_tc_config(const bokt_params* p, bool grouped, int experts, int smem_optin,
+                      TcConfig* out) {
+  const bokt_params zero = {};
+  if (!p) p = &zero;
+  const int bm = param_or(p->block_m, 128);
+  const int bk = param_or(p->block_k, 64);
+  const int bn = param_or(p->block_n, 256);
+  const int warps = param_or(p->num_warps, 6);
+  if (bm != 128) return fail(BOKT_ERR_CONFIG, "block_m must be 128 (tcgen05 cta_group::1 M)");
+  if (bk != 64) return fail(BOKT_ERR_CONFIG, "block_k must be 64 (one 128-byte swizzle row)");
+  if (bn != 64 && bn != 128 && bn != 256)
+    return fail(BOKT_ERR_CONFIG, "block_n must be 64, 128 or 256 (got %d)", bn);
+  if (warps != 6) return fail(BOKT_ERR_CONFIG, "num_warps must be 6 (TMA, MMA, 4 epilogue)");
+  if (p->split_k > 1) return fail(BOKT_ERR_UNSUPPORTED, "split_k > 1 is not implemented");
+  if (p->cta_group > 1) return fail(BOKT_ERR_UNSUPPORTED, "cta_group 2 is not implemented");
+  const int stages = param_or(p->stages, bn == 256 ? 4 : 6);
+  if (stages < 2 || stages > 8) return fail(BOKT_ERR_CONFIG, "stages must be in [2, 8]");
+  int smem = bokt::gemm_tc_smem_bytes(bn, stages, grouped, experts);
+  if (smem > smem_optin)
+    return fail(BOKT_ERR_CONFIG, "block_n=%d stages=%d needs %d bytes of shared memory (max %d)",
+                bn, stages, smem, smem_optin);
+  // One CTA per SM: the persistent schedule assumes it and two CTAs would
+  // contend for the 512 TMEM columns.
+  const int one_per_sm = smem_optin / 2 + 1024;
+  if (smem < one_per_sm) smem = one_per_sm;
+  out->bn = bn;
+  out->stages = stages;
+  out->group_m = param_or(p->group_m, 8);
+  out->smem = smem;
+  return BOKT_OK;
+}
+
+int launch_tc(bool grouped, int dtype, const TcConfig& cfg, const CUtensorMap& ma,
+              const CUtensorMap& mb, const GemmTcArgs& args, int grid, cudaStream_t s) {
+  const void* fn = tc_kernel(grouped, dtype, cfg.bn);
+  int rc = ensure_smem(fn, cfg.smem);
+  if (rc) return rc;
+  void* kargs[] = {const_cast<CUtensorMap*>(&ma), const_cast<CUtensorMap*>(&mb),
+                   const_cast<GemmTcArgs*>(&args)};
+  cudaError_t e = cudaLaunchKernel(fn, dim3(grid), dim3(bokt::kGemmThreads), kargs, cfg.smem, s);
+  if (e != cudaSuccess) return cuda_fail(e, "gemm_tc launch");
+  return BOKT_OK;
+}
+
+template <typename T>
+int launch_simt(const void* A, const void* B, void* C, int rows, int N, int K,
+                const void* offsets, int offsets_i64, int experts, cudaStream_t s) {
+  dim3 grid((N + bokt::kSimtCols - 1) / bokt::kSimtCols, rows < 65535 ? rows : 65535);
+  bokt::gemm_simt_kernel<T><<<grid, bokt::kSimtCols, 0, s>>>(
+      static_cast<const T*>(A), static_cast<const T*>(B), static_cast<T*>(C), rows, N, K, offsets,
+      offsets_i64, experts);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gemm_simt launch");
+  return BOKT_OK;
+}
+
+bool tc_eligible(const void* A, const void* B, const void* C, int N, int K) {
+  return K > 0 && (K % 8) == 0 && (N % 8) == 0 && aligned16(A) && aligned16(B) && aligned16(C);
+}
+
+// ----------------------------------------------------------------- RMSNorm dispatch
+struct NormConfig {
+  int rows_per_cta, threads, tpr_log2, vpt;  // vpt 0 = generic kernel
+};
+
+int resolve_norm_config(const bokt_params* p, int N, bool vec_ok, NormConfig* out) {
+  const bokt_params zero = {};
+  if (!p) p = &zero;
+  const int rows = param_or(p->rows_per_cta, 1);
+  const int warps = param_or(p->num_warps, 4);
+  if (warps != 1 && warps != 2 && warps != 4 && warps != 8 && warps != 16 && warps != 32)
+    return fail(BOKT_ERR_CONFIG, "num_warps must be a power of two <= 32 (got %d)", warps);
+  if (rows != 1 && rows != 2 && rows != 4 && rows != 8 && rows != 16)
+    return fail(BOKT_ERR_CONFIG, "rows_per_cta must be 1, 2, 4, 8 or 16 (got %d)", rows);
+  const int threads = warps * 32;
+  if (rows > threads) return fail(BOKT_ERR_CONFIG, "rows_per_cta exceeds threads per CTA");
+  const int tpr = threads / rows;
+  int lg = 0;
+  while ((1 << lg) < tpr) ++lg;
+  int vpt = 0;
+  if (vec_ok) {
+    const int nvec = N / 8;
+    const int need = (nvec + tpr - 1) / tpr;
+    int v = 1;
+    while (v < need) v <<= 1;
+    if (v <= 16) vpt = v;
+  }
+  *out = {rows, threads, lg, vpt};
+  return BOKT_OK;
+}
+
+template <typename T>
+const void* norm_kernel(int vpt) {
+  switch (vpt) {
+    case 0: return reinterpret_cast<const void*>(&bokt::rmsnorm_generic_kernel<T>);
+    case 1: return reinterpret_cast<const void*>(&bokt::rmsnorm_vec_kernel<T, 1>);
+    case 2: return reinterpret_cast<const void*>(&bokt::rmsnorm_vec_kernel<T, 2>);
+    case 4: return reinterpret_cast<const void*>(&bokt::rmsnorm_vec_kernel<T, 4>);
+    case 8: return reinterpret_cast<const void*>(&bokt::rmsnorm_vec_kernel<T, 8>);
+    case 16: return reinterpret_cast<const void*>(&bokt::rmsnorm_vec_kernel<T, 16>);
+  }
+  return nullptr;
+}
+
+}  // namespace
+
+// =================================================================== C ABI
+extern "C" {
+
+int bokt_abi_version(void) { return BOKT_ABI_VERSION; }
+
+int bokt_built_sm(void) { return 100; }
+
+const char* bokt_last_error(void) { return g_err; }
+
+int bokt_gemm(const void* A, const void* B, void* C, int M, int N, int K, int dtype,
+              const bokt_params* params, void* stream) {
+  g_err[0] = 0;
+  if (dtype != BOKT_FP16 && dtype != BOKT_BF16) return fail(BOKT_ERR_INVALID, "dtype %d", dtype);
+  if (M < 0 || N < 0 || K < 0) return fail(BOKT_ERR_INVALID, "negative size");
+  if (M == 0 || N == 0) return BOKT_OK;
+  if (!A || !B || !C) return fail(BOKT_ERR_INVALID, "null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DeviceInfo dev;
+  int rc = device_info(&dev);
+  if (rc) return rc;
+  if (!tc_eligible(A, B, C, N, K)) {
+    return dtype == BOKT_BF16 ? launch_simt<__nv_bfloat16>(A, B, C, M, N, K, nullptr, 0, 0, s)
+                              : launch_simt<__half>(A, B, C, M, N, K, nullptr, 0, 0, s);
+  }
+  TcConfig cfg;
+  rc = resolve_tc_config(params, false, 0, dev.smem_optin, &cfg);
+  if (rc) return rc;
+  CUtensorMap ma, mb;
+  const uint64_t da[2] = {uint64_t(K), uint64_t(M)};
+  const uint64_t sa[1] = {uint64_t(K) * 2};
+  const uint32_t ba[2] = {64, 128};
+  rc = encode_map(&ma, A, 2, da, sa, ba, dtype == BOKT_FP16);
+  if (rc) return rc;
+  const uint64_t db[2] = {uint64_t(N), uint64_t(K)};
+  const uint64_t sb[1] = {uint64_t(N) * 2};
+  const uint32_t bb[2] = {64, 64};
+  rc = encode_map(&mb, B, 2, db, sb, bb, dtype == BOKT_FP16);
+  if (rc) return rc;
+  GemmTcArgs args = {};
+  args.C = C;
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.group_m = cfg.group_m;
+  args.stages = cfg.stages;
+  args.idesc = bokt::make_idesc_f16(uint32_t(dtype), 128, uint32_t(cfg.bn));
+  const long long tiles = (long long)((M + 127) / 128) * ((N + cfg.bn - 1) / cfg.bn);
+  const int grid = int(tiles < dev.sm_count ? tiles : dev.sm_count);
+  return launch_tc(false, dtype, cfg, ma, mb, args, grid, s);
+}
+
+int bokt_moe_grouped_gemm(const void* X, const void* W, const void* offsets, int offsets_is_i64,
+                          void* Y, int T, int E, int N, int K, int dtype, int sm_count,
+                          const bokt_params* params, void* stream) {
+  g_err[0] = 0;
+  if (dtype != BOKT_FP16 && dtype != BOKT_BF16) return fail(BOKT_ERR_INVALID, "dtype %d", dtype);
+  if (T < 0 || E < 0 || N < 0 || K < 0) return fail(BOKT_ERR_INVALID, "negative size");
+  if (E > bokt::kGemmMaxExperts)
+    return fail(BOKT_ERR_UNSUPPORTED, "at most %d experts", bokt::kGemmMaxExperts);
+  if (T == 0 || E == 0 || N == 0) return BOKT_OK;
+  if (!X || !W || !Y || !offsets) return fail(BOKT_ERR_INVALID, "null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DeviceInfo dev;
+  int rc = device_info(&dev);
+  if (rc) return rc;
+  if (!tc_eligible(X, W, Y, N, K)) {
+    return dtype == BOKT_BF16
+               ? launch_simt<__nv_bfloat16>(X, W, Y, T, N, K, offsets, offsets_is_i64, E, s)
+               : launch_simt<__half>(X, W, Y, T, N, K, offsets, offsets_is_i64, E, s);
+  }
+  TcConfig cfg;
+  rc = resolve_tc_config(params, true, E, dev.smem_optin, &cfg);
+  if (rc) return rc;
+  CUtensorMap ma, mb;
+  const uint64_t da[2] = {uint64_t(K), uint64_t(T)};
+  const uint64_t sa[1] = {uint64_t(K) * 2};
+  const uint32_t ba[2] = {64, 128};
+  rc = encode_map(&ma, X, 2, da, sa, ba, dtype == BOKT_FP16);
+  if (rc) return rc;
+  const uint64_t db[3] = {uint64_t(N), uint64_t(K), uint64_t(E)};
+  const uint64_t sb[2] = {uint64_t(N) * 2, uint64_t(K) * uint64_t(N) * 2};
+  const uint32_t bb[3] = {64, 64, 1};
+  rc = encode_map(&mb, W, 3, db, sb, bb, dtype == BOKT_FP16);
+  if (rc) return rc;
+  GemmTcArgs args = {};
+  args.C = Y;
+  args.M = T;
+  args.N = N;
+  args.K = K;
+  args.group_m = 1;
+  args.stages = cfg.stages;
+  args.idesc = bokt::make_idesc_f16(uint32_t(dtype), 128, uint32_t(cfg.bn));
+  args.offsets = offsets;
+  args.offsets_i64 = offsets_is_i64 ? 1 : 0;
+  args.E = E;
+  const bokt_params zero = {};
+  const int mult = param_or((params ? params : &zero)->cta_multiplier, 1);
+  const int sms = sm_count > 0 ? sm_count : dev.sm_count;
+  // Upper bound on tiles without reading offsets: sum_e cdiv(c_e, 128) <= cdiv(T, 128) + E.
+  const long long max_tiles = ((long long)(T + 127) / 128 + E) * ((N + cfg.bn - 1) / cfg.bn);
+  long long grid = (long long)sms * mult;
+  if (grid > max_tiles) grid = max_tiles;
+  if (grid < 1) grid = 1;
+  return launch_tc(true, dtype, cfg, ma, mb, args, int(grid), s);
+}
+
+int bokt_rmsnorm(const void* X, const void* W, void* Y, int M, int N, float eps, int dtype,
+                 const bokt_params* params, void* stream) {
+  g_err[0] = 0;
+  if (dtype != BOKT_FP16 && dtype != BOKT_BF16) return fail(BOKT_ERR_INVALID, "dtype %d", dtype);
+  if (M < 0 || N < 0) return fail(BOKT_ERR_INVALID, "negative size");
+  if (M == 0 || N == 0) return BOKT_OK;
+  if (!X || !W || !Y) return fail(BOKT_ERR_INVALID, "null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool vec_ok = (N % 8) == 0 && aligned16(X) && aligned16(W) && aligned16(Y);
+  NormConfig cfg;
+  int rc = resolve_norm_config(params, N, vec_ok, &cfg);
+  if (rc) return rc;
+  const int grid = (M + cfg.rows_per_cta - 1) / cfg.rows_per_cta;
+  const void* fn = dtype == BOKT_BF16 ? norm_kernel<__nv_bfloat16>(cfg.vpt)
+                                      : norm_kernel<__half>(cfg.vpt);
+  void* kargs[] = {const_cast<void**>(&X), const_cast<void**>(&W), &Y, &M, &N, &eps,
+                   &cfg.rows_per_cta, &cfg.tpr_log2};
+  cudaError_t e = cudaLaunchKernel(fn, dim3(grid), dim3(cfg.threads), kargs, 0, s);
+  if (e != cudaSuccess) return cuda_fail(e, "rmsnorm launch");
+  return BOKT_OK;
+}
+
+int64_t bokt_moe_route_workspace_bytes(int A, int E) {
+  if (A < 0 || E <= 0) return 0;
+  const int64_t chunks = (A + bokt::kRouteChunk - 1) / bokt::kRouteChunk;
+  return (chunks > 0 ? chunks : 1) * int64_t(E) * 4;
+}
+
+int bokt_moe_route(const int32_t* expert_ids, int A, int E, int32_t* counts, int32_t* offsets,
+                   int64_t* offsets64, int32_t* perm, int32_t* inv_perm, void* workspace,
+                   int64_t workspace_bytes, void* stream) {
+  g_err[0] = 0;
+  if (A < 0 || E <= 0) return fail(BOKT_ERR_INVALID, "need A >= 0 and E > 0");
+  if (E > bokt::kRouteMaxExperts)
+    return fail(BOKT_ERR_UNSUPPORTED, "at most %d experts", bokt::kRouteMaxExperts);
+  if (!counts || !offsets || (A > 0 && (!expert_ids || !perm || !inv_perm)))
+    return fail(BOKT_ERR_INVALID, "null pointer");
+  if (workspace_bytes < bokt_moe_route_workspace_bytes(A, E) || !workspace)
+    return fail(BOKT_ERR_INVALID, "workspace too small: need %lld bytes",
+                (long long)bokt_moe_route_workspace_bytes(A, E));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int chunks = (A + bokt::kRouteChunk - 1) / bokt::kRouteChunk;
+  int32_t* ws = static_cast<int32_t*>(workspace);
+  if (chunks > 0)
+    bokt::route_count_kernel<<<chunks, bokt::kRouteThreads, 0, s>>>(expert_ids, A, E, ws);
+  bokt::route_scan_kernel<<<1, 1024, 0, s>>>(ws, chunks, E, counts, offsets,
+                                             reinterpret_cast<long long*>(offsets64));
+  if (chunks > 0)
+    bokt::route_scatter_kernel<<<chunks, bokt::kRouteThreads, 0, s>>>(expert_ids, A, E, ws, perm,
+                                                                      inv_perm);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "moe_route launch");
+  return BOKT_OK;
+}
+
+int bokt_gather_rows(const void* src, int64_t src_rows, void* dst, const int32_t* index, int rows,
+                     int cols, int elem_bytes, int divisor, void* stream) {
+  g_err[0] = 0;
+  if (rows < 0 || cols < 0 || src_rows < 0 || divisor <= 0 || elem_bytes <= 0)
+    return fail(BOKT_ERR_INVALID, "bad size");
+  if (rows == 0 || cols == 0) return BOKT_OK;
+  if (!src || !dst || !index) return fail(BOKT_ERR_INVALID, "null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const long long row_bytes = (long long)cols * elem_bytes;
+  const int grid = rows < 65535 * 4 ? rows : 65535 * 4;
+  if (row_bytes % 16 == 0 && aligned16(src) && aligned16(dst)) {
+    const int vecs = int(row_bytes / 16);
+    bokt::gather_rows_kernel<uint4><<<grid, 128, 0, s>>>(
+        static_cast<const uint4*>(src), src_rows, static_cast<uint4*>(dst), index, rows, vecs,
+        divisor);
+  } else {
+    bokt::gather_rows_kernel<uint8_t><<<grid, 128, 0, s>>>(
+        static_cast<const uint8_t*>(src), src_rows, static_cast<uint8_t*>(dst), index, rows,
+        int(row_bytes), divisor);
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "gather_rows launch");
+  return BOKT_OK;
+}
+
+int bokt_kernel_attrs(int kernel, int dtype, int n, int k, const bokt_params* params,
+                      bokt_attrs* out) {
+  g_err[0] = 0;
+  if (!out) return fail(BOKT_ERR_INVALID, "null output");
+  if (dtype != BOKT_FP16 && dtype != BOKT_BF16) return fail(BOKT_ERR_INVALID, "dtype %d", dtype);
+  DeviceInfo dev;
+  int rc = device_info(&dev);
+  if (rc) return rc;
+  const void* fn = nullptr;
+  int dyn = 0, threads = 0, path = 0;
+  if (kernel == BOKT_KERNEL_GEMM || kernel == BOKT_KERNEL_MOE_GROUPED_GEMM) {
+    const bool grouped = kernel == BOKT_KERNEL_MOE_GROUPED_GEMM;
+    if ((n % 8) == 0 && (k % 8) == 0 && k > 0) {
+      TcConfig cfg;
+      rc = resolve_tc_config(params, grouped, grouped ? 64 : 0, dev.smem_optin, &cfg);
+      if (rc) return rc;
+      fn = tc_kernel(grouped, dtype, cfg.bn);
+      dyn = cfg.smem;
+      threads = bokt::kGemmThreads;
+      path = 0;
+    } else {
+      fn = dtype == BOKT_BF16 ? reinterpret_cast<const void*>(&bokt::gemm_simt_kernel<__nv_bfloat16>)
+                              : reinterpret_cast<const void*>(&bokt::gemm_simt_kernel<__half>);
+      threads = bokt::kSimtCols;
+      path = 1;
+    }
+  } else if (kernel == BOKT_KERNEL_RMSNORM) {
+    NormConfig cfg;
+    rc = resolve_norm_config(params, n, (n % 8) == 0, &cfg);
+    if (rc) return rc;
+    fn = dtype == BOKT_BF16 ? norm_kernel<__nv_bfloat16>(cfg.vpt) : norm_kernel<__half>(cfg.vpt);
+    threads = cfg.threads;
+    path = cfg.vpt ? 2 : 3;
+  } else {
+    return fail(BOKT_ERR_INVALID, "unknown kernel id %d", kernel);
+  }
+  cudaFuncAttributes a;
+  cudaError_t e = cudaFuncGetAttributes(&a, fn);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncGetAttributes");
+  out->shared_bytes = int(a.sharedSizeBytes) + dyn;
+  out->registers = a.numRegs;
+  out->local_bytes = int(a.localSizeBytes);
+  out->threads = threads;
+  out->max_threads = a.maxThreadsPerBlock;
+  out->path = path;
+  return BOKT_OK;
+}
+
+int bokt_device_status(int* code, int* detail, int reset) {
+  g_err[0] = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  int h[2] = {0, 0};
+  e = cudaMemcpyFromSymbol(h, bokt::g_status, sizeof(h));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyFromSymbol(status)");
+  if (code) *code = h[0];
+  if (detail) *detail = h[1];
+  if (reset) {
+    const int z[2] = {0, 0};
+    e = cudaMemcpyToSymbol(bokt::g_status, z, sizeof(z));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyToSymbol(status)");
+  }
+  return BOKT_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,329 @@
+// tcgen05 GEMM for sm_100a: C = A * B with A [rows, K] K-major and B [K, N]
+// N-major (both row-major in HBM), fp16/bf16 operands, fp32 accumulation in
+// TMEM, rounded to the operand type on store.
+//
+// One kernel body serves both operators of the reference:
+//   dense   : kernels/gemm.py:7-40            (GROUP_M raster, masked edges)
+//   grouped : kernels/moe_grouped_gemm.py:11-58 (ragged experts, one persistent
+//             launch, empty experts cost nothing, every output tile has one writer)
+//
+// CTA = 6 warps, persistent over a static tile schedule (tile += gridDim.x):
+//   warp 0    : TMA producer (one lane) filling a `stages`-deep smem ring
+//   warp 1    : TMEM allocator + MMA issuer (one lane), 128 x BN x 16 per MMA
+//   warps 2-5 : epilogue; warp w drains TMEM lanes 32*(w%4)..+31 (= tile rows)
+// Two TMEM accumulators (2 x BN fp32 columns) let the epilogue of tile i
+// overlap the main loop of tile i+1.  Operand tiles use the 128-byte swizzle:
+// A tile = 128 rows x 64 K (16 KB), B tile = 64 K rows x BN (BN/64 boxes of
+// 64 x 64).  No cluster launch and no multicast.
+#pragma once
+
+#include "bokt_device.cuh"
+
+namespace bokt {
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBK = 64;
+constexpr int kGemmThreads = 192;
+constexpr int kGemmABytes = kGemmBM * kGemmBK * 2;  // 16 KB per stage
+constexpr int kGemmMaxExperts = 4096;
+
+struct GemmTcArgs {
+  void* C;
+  int M;        // dense: rows of A/C.  grouped: T (rows of X/Y)
+  int N;
+  int K;
+  int group_m;  // dense raster width (tiles of M per group)
+  int stages;
+  uint32_t idesc;
+  const void* offsets;  // grouped only: E+1 offsets
+  int offsets_i64;
+  int E;
+};
+
+template <int BN>
+struct GemmTcShape {
+  static constexpr int kBBytes = BN * kGemmBK * 2;
+  static constexpr int kStageBytes = kGemmABytes + kBBytes;
+  static constexpr int kTmemCols = 2 * BN;
+  static_assert(BN == 64 || BN == 128 || BN == 256, "BN must be 64, 128 or 256");
+};
+
+// Dynamic shared memory the kernel needs (host and device agree on this).
+__host__ __device__ inline int gemm_tc_smem_bytes(int bn, int stages, bool grouped, int experts) {
+  int bytes = 1024 /* alignment slack */ + stages * (kGemmABytes + bn * kGemmBK * 2) +
+              (2 * stages + 4) * 8 + 16;
+  if (grouped) bytes += (3 * experts + 1) * 4;
+  return bytes;
+}
+
+struct TileCoord {
+  int a_row;       // first row of the A / X box
+  int n0;          // first column of the tile
+  int expert;      // grouped only
+  int c_row;       // first row of C / Y written by this tile
+  int rows_valid;  // rows of this tile inside the problem (<= 128)
+};
+
+__device__ __forceinline__ TileCoord dense_tile(int t, int M, int nn, int group_m, int bn) {
+  // GROUP_M rasterisation, same mapping as kernels/gemm.py:20-26.
+  const int nm = (M + kGemmBM - 1) / kGemmBM;
+  const int per_group = group_m * nn;
+  const int group = t / per_group;
+  const int first_m = group * group_m;
+  const int gm = min(nm - first_m, group_m);
+  const int local = t - group * per_group;
+  const int pm = first_m + local % gm;
+  const int pn = local / gm;
+  TileCoord c;
+  c.a_row = pm * kGemmBM;
+  c.n0 = pn * bn;
+  c.expert = 0;
+  c.c_row = c.a_row;
+  c.rows_valid = min(kGemmBM, M - c.a_row);
+  return c;
+}
+
+__device__ __forceinline__ TileCoord grouped_tile(int t, const int* tile_prefix,
+                                                  const int* row_start, const int* row_count,
+                                                  int E, int nn, int bn) {
+  // Largest e with tile_prefix[e] <= t (tile_prefix is non-decreasing, t < tile_prefix[E]).
+  int lo = 0, hi = E - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (tile_prefix[mid] <= t) lo = mid;
+    else hi = mid - 1;
+  }
+  const int e = lo;
+  const int rel = t - tile_prefix[e];
+  const int count = row_count[e];
+  const int mblocks = (count + kGemmBM - 1) / kGemmBM;
+  // M fastest inside an expert: all row blocks of one weight column block run
+  // together, so W[e][:, n-block] is fetched from HBM once and reused from L2.
+  const int mb = rel % mblocks;
+  const int nb = rel / mblocks;
+  TileCoord c;
+  c.a_row = row_start[e] + mb * kGemmBM;
+  c.n0 = nb * bn;
+  c.expert = e;
+  c.c_row = c.a_row;
+  c.rows_valid = min(kGemmBM, count - mb * kGemmBM);
+  return c;
+}
+
+template <int BN, bool GROUPED, typename OutT>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   GemmTcArgs args) {
+  using Shape = GemmTcShape<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+
+  const int stages = args.stages;
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + stages * kGemmABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + stages * Shape::kBBytes);
+  uint64_t* empty = full + stages;
+  uint64_t* tfull = empty + stages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  int* tile_prefix = reinterpret_cast<int*>(tmem_holder + 4);  // [E+1], grouped only
+  int* row_start = tile_prefix + (args.E + 1);                 // [E]
+  int* row_count = row_start + args.E;                         // [E]
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int N = args.N;
+  const int nn = (N + BN - 1) / BN;
+  const int nkb = (args.K + kGemmBK - 1) / kGemmBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4 * 32);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, Shape::kTmemCols);
+    tmem_relinquish();
+  }
+
+  int ntiles;
+  if constexpr (GROUPED) {
+    const int E = args.E;
+    const int T = args.M;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+      long long s, t;
+      if (args.offsets_i64) {
+        s = reinterpret_cast<const long long*>(args.offsets)[e];
+        t = reinterpret_cast<const long long*>(args.offsets)[e + 1];
+      } else {
+        s = reinterpret_cast<const int*>(args.offsets)[e];
+        t = reinterpret_cast<const int*>(args.offsets)[e + 1];
+      }
+      s = s < 0 ? 0 : (s > T ? T : s);
+      t = t < s ? s : (t > T ? T : t);
+      row_start[e] = static_cast<int>(s);
+      row_count[e] = static_cast<int>(t - s);
+      tile_prefix[e + 1] = static_cast<int>((t - s + kGemmBM - 1) / kGemmBM) * nn;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      tile_prefix[0] = 0;
+      for (int e = 0; e < E; ++e) tile_prefix[e + 1] += tile_prefix[e];
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  if constexpr (GROUPED) {
+    ntiles = tile_prefix[args.E];
+  } else {
+    ntiles = ((args.M + kGemmBM - 1) / kGemmBM) * nn;
+  }
+
+  auto tile_at = [&](int t) -> TileCoord {
+    if constexpr (GROUPED) {
+      return grouped_tile(t, tile_prefix, row_start, row_count, args.E, nn, BN);
+    } else {
+      return dense_tile(t, args.M, nn, args.group_m, BN);
+    }
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        const TileCoord tc = tile_at(t);
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, 1)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], Shape::kStageBytes);
+          uint8_t* a_dst = sA + stage * kGemmABytes;
+          uint8_t* b_dst = sB + stage * Shape::kBBytes;
+          tma_load_2d(a_dst, &tmA, &full[stage], kb * kGemmBK, tc.a_row);
+#pragma unroll
+          for (int c = 0; c < BN / 64; ++c) {
+            if constexpr (GROUPED) {
+              tma_load_3d(b_dst + c * 8192, &tmB, &full[stage], tc.n0 + c * 64, kb * kGemmBK,
+                          tc.expert);
+            } else {
+              tma_load_2d(b_dst + c * 8192, &tmB, &full[stage], tc.n0 + c * 64, kb * kGemmBK);
+            }
+          }
+          if (++stage == stages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int i = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++i) {
+        const int acc = i & 1;
+        const uint32_t acc_phase = (static_cast<uint32_t>(i) >> 1) & 1u;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, 2)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, 3)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_addr(sA + stage * kGemmABytes);
+          const uint32_t b_addr = smem_addr(sB + stage * Shape::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kGemmBK / 16; ++k) {
+            // A: K-major, 128-byte rows; a K16 step is 32 bytes along the row.
+            const uint64_t a_desc = smem_desc_sw128(a_addr + k * 32, 16, 1024);
+            // B: N-major; a K16 step is two 8-row groups (2 x 1024 bytes);
+            // 64-column boxes sit 64 rows x 128 bytes apart.
+            const uint64_t b_desc = smem_desc_sw128(b_addr + k * 2048, 64 * 128, 1024);
+            umma_f16_ss(d_tmem, a_desc, b_desc, args.idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == stages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int r = q * 32 + lane;
+    OutT* C = reinterpret_cast<OutT*>(args.C);
+    int i = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+      const TileCoord tc = tile_at(t);
+      const int acc = i & 1;
+      const uint32_t acc_phase = (static_cast<uint32_t>(i) >> 1) & 1u;
+      const bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, 4);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const uint32_t taddr =
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      const bool row_ok = r < tc.rows_valid;
+      OutT* crow = C + static_cast<size_t>(tc.c_row + (row_ok ? r : 0)) * N + tc.n0;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c), v);
+        tmem_ld_wait();
+        if (row_ok) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            if (tc.n0 + c + j < N) {  // N % 8 == 0 on this path: 8-column chunks are all-or-none
+              uint4 pk;
+              pk.x = Pack2<OutT>::pack(__uint_as_float(v[j + 0]), __uint_as_float(v[j + 1]));
+              pk.y = Pack2<OutT>::pack(__uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+              pk.z = Pack2<OutT>::pack(__uint_as_float(v[j + 4]), __uint_as_float(v[j + 5]));
+              pk.w = Pack2<OutT>::pack(__uint_as_float(v[j + 6]), __uint_as_float(v[j + 7]));
+              *reinterpret_cast<uint4*>(crow + c + j) = pk;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  // ---------------------------------------------------------------- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Shape::kTmemCols);
+  }
+}
+
+}  // namespace bokt

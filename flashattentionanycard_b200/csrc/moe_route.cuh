@@ -1,0 +1,176 @@
+// MoE routing front end: expert histogram -> offsets (exclusive prefix sum) ->
+// stable permutation of assignments by expert -> inverse permutation (combine
+// indices), plus the row gather that packs token activations in expert order.
+//
+// The reference builds offsets on the host (tuner/worker.py:81-86) and leaves
+// routing outside the operator (kernels/moe_grouped_gemm.py:3).  Here the
+// whole front end is device resident so the grouped GEMM reads offsets that a
+// kernel produced (no host round trip, graph-capturable).  Integer work,
+// bit-exact against a stable counting sort:
+//   counts[e]   = #{i : id[i] == e}
+//   offsets[e]  = sum_{e' < e} counts[e']
+//   perm[j]     = i  such that i is the (j - offsets[e])-th assignment of expert e
+//   inv_perm[i] = j
+//
+// Three launches over chunks of kRouteChunk assignments:
+//   1. route_count   : per-chunk expert histogram (shared-memory atomics; order
+//                      independent, so deterministic)
+//   2. route_scan    : one CTA; column prefix over chunks + exclusive scan over
+//                      experts -> counts, offsets, per-(chunk, expert) base rows
+//   3. route_scatter : each chunk walks its assignments in order, 256 at a time;
+//                      rank inside a warp from __match_any_sync, across warps from
+//                      a per-warp count table -> stable destinations
+#pragma once
+
+#include "bokt_device.cuh"
+
+namespace bokt {
+
+constexpr int kRouteChunk = 4096;
+constexpr int kRouteThreads = 256;
+constexpr int kRouteWarps = kRouteThreads / 32;
+constexpr int kRouteMaxExperts = 1024;
+
+__global__ void __launch_bounds__(kRouteThreads) route_count_kernel(const int32_t* __restrict__ ids,
+                                                                     int A, int E,
+                                                                     int32_t* __restrict__ chunk_counts) {
+  __shared__ int hist[kRouteMaxExperts];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
+  __syncthreads();
+  const int begin = blockIdx.x * kRouteChunk;
+  const int end = min(A, begin + kRouteChunk);
+  for (int i = begin + threadIdx.x; i < end; i += blockDim.x) {
+    const int e = ids[i];
+    if (e >= 0 && e < E) atomicAdd(&hist[e], 1);
+    else report_status(kStatusBadExpertId, i);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x)
+    chunk_counts[static_cast<size_t>(blockIdx.x) * E + e] = hist[e];
+}
+
+// One CTA of 1024 threads.  chunk_counts[c][e] is replaced by the first packed
+// row of chunk c's assignments to expert e.
+__global__ void __launch_bounds__(1024) route_scan_kernel(int32_t* __restrict__ chunk_counts,
+                                                          int chunks, int E,
+                                                          int32_t* __restrict__ counts,
+                                                          int32_t* __restrict__ offsets,
+                                                          long long* __restrict__ offsets64) {
+  __shared__ int totals[kRouteMaxExperts];
+  __shared__ int warp_sums[32];
+  __shared__ int carry;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int run = 0;
+    for (int c = 0; c < chunks; ++c) {
+      const int v = chunk_counts[static_cast<size_t>(c) * E + e];
+      chunk_counts[static_cast<size_t>(c) * E + e] = run;  // exclusive column prefix
+      run += v;
+    }
+    totals[e] = run;
+    counts[e] = run;
+  }
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  // Exclusive scan of totals over experts, 1024 at a time.
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int base = 0; base < E; base += blockDim.x) {
+    const int e = base + threadIdx.x;
+    const int v = e < E ? totals[e] : 0;
+    int incl = v;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      int w = warp_sums[lane];
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += n;
+      }
+      warp_sums[lane] = w;  // inclusive over warps
+    }
+    __syncthreads();
+    const int excl = carry + (warp > 0 ? warp_sums[warp - 1] : 0) + incl - v;
+    if (e < E) {
+      offsets[e] = excl;
+      if (offsets64) offsets64[e] = excl;
+    }
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) carry = excl + v;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    offsets[E] = carry;
+    if (offsets64) offsets64[E] = carry;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    const int off = offsets[e];
+    for (int c = 0; c < chunks; ++c) chunk_counts[static_cast<size_t>(c) * E + e] += off;
+  }
+}
+
+__global__ void __launch_bounds__(kRouteThreads) route_scatter_kernel(
+    const int32_t* __restrict__ ids, int A, int E, const int32_t* __restrict__ chunk_base,
+    int32_t* __restrict__ perm, int32_t* __restrict__ inv_perm) {
+  __shared__ int running[kRouteMaxExperts];
+  __shared__ int wcnt[kRouteWarps][kRouteMaxExperts];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    running[e] = chunk_base[static_cast<size_t>(blockIdx.x) * E + e];
+    for (int w = 0; w < kRouteWarps; ++w) wcnt[w][e] = 0;
+  }
+  __syncthreads();
+  const unsigned lt_mask = (1u << lane) - 1u;
+  const int begin = blockIdx.x * kRouteChunk;
+  const int end = min(A, begin + kRouteChunk);
+  for (int base = begin; base < end; base += kRouteThreads) {
+    const int i = base + threadIdx.x;
+    int e = (i < end) ? ids[i] : -1;
+    if (e < 0 || e >= E) e = -1;  // invalid ids were reported by route_count
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int rank = __popc(peers & lt_mask);
+    const bool leader = (peers & lt_mask) == 0;
+    if (e >= 0 && leader) wcnt[warp][e] = __popc(peers);
+    __syncthreads();
+    int dest = 0;
+    if (e >= 0) {
+      int pre = 0;
+      for (int w = 0; w < warp; ++w) pre += wcnt[w][e];
+      dest = running[e] + pre + rank;
+    }
+    __syncthreads();
+    if (e >= 0 && leader) {
+      atomicAdd(&running[e], __popc(peers));
+      wcnt[warp][e] = 0;
+    }
+    if (e >= 0) {
+      perm[dest] = i;
+      inv_perm[i] = dest;
+    }
+    __syncthreads();
+  }
+}
+
+// dst[j, :] = src[index[j] / divisor, :]; one CTA slice per row, 16-byte
+// vectors when the row length and both bases allow it.
+template <typename V>
+__global__ void gather_rows_kernel(const V* __restrict__ src, long long src_rows, V* __restrict__ dst,
+                                   const int32_t* __restrict__ index, int rows, int row_vecs,
+                                   int divisor) {
+  for (int j = blockIdx.x; j < rows; j += gridDim.x) {
+    const int raw = index[j];
+    const long long s = raw / divisor;
+    if (raw < 0 || s >= src_rows) {
+      if (threadIdx.x == 0) report_status(kStatusBadExpertId, j);
+      continue;
+    }
+    const V* sr = src + s * row_vecs;
+    V* dr = dst + static_cast<long long>(j) * row_vecs;
+    for (int c = threadIdx.x; c < row_vecs; c += blockDim.x) dr[c] = sr[c];
+  }
+}
+
+}  // namespace bokt

@@ -1,0 +1,169 @@
+/*
+ * bokt.h - C ABI of the sm_100a (B200) kernels behind the bo-kernel-tuner
+ * operator interface: dense GEMM, fused RMSNorm, MoE grouped GEMM and the
+ * device-side MoE routing front end (expert histogram, offsets, stable token
+ * permutation, combine indices).
+ *
+ * Every entry point takes plain device pointers, integer sizes and an opaque
+ * CUDA stream (cudaStream_t passed as void*; NULL = legacy default stream).
+ * Nothing here allocates device memory, synchronises the stream or reads a
+ * result back, so every compute call can be captured in a CUDA graph once the
+ * first call for a given configuration has run (the first call sets kernel
+ * attributes).  Return value: 0 on success, a BOKT_ERR_* code otherwise; the
+ * message is available from bokt_last_error() on the calling thread.
+ *
+ * Reference interfaces replaced (paths inside the reference project):
+ *   bokt_gemm               <- bo_kernel_tuner/kernels/gemm.py:43-48  launch(a, b, out, params)
+ *   bokt_rmsnorm            <- bo_kernel_tuner/kernels/rmsnorm.py:29-33 launch(x, weight, out, params, epsilon)
+ *   bokt_moe_grouped_gemm   <- bo_kernel_tuner/kernels/moe_grouped_gemm.py:61-65
+ *                              launch(x, weights, offsets, out, params, sm_count)
+ *   bokt_moe_route          <- bo_kernel_tuner/tuner/worker.py:81-86 (host prefix sum of
+ *                              expert token counts -> offsets); the permutation and combine
+ *                              indices have no counterpart in the reference
+ *                              (kernels/moe_grouped_gemm.py:3 leaves routing outside)
+ *   bokt_gather_rows        <- no counterpart (packing tokens in expert order)
+ *   bokt_kernel_attrs       <- the Triton compiled-kernel metadata read by
+ *                              bo_kernel_tuner/tuner/worker.py:193,203-204
+ *                              (metadata.shared, n_regs, n_spills)
+ */
+#ifndef BOKT_H_
+#define BOKT_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BOKT_ABI_VERSION 1
+
+/* element types (values match the tcgen05 kind::f16 operand format codes) */
+#define BOKT_FP16 0
+#define BOKT_BF16 1
+
+/* status codes */
+#define BOKT_OK 0
+#define BOKT_ERR_INVALID 1     /* bad argument: null pointer, negative size, ... */
+#define BOKT_ERR_UNSUPPORTED 2 /* legal request this build does not implement */
+#define BOKT_ERR_CONFIG 3      /* launch parameters outside the kernel's domain */
+#define BOKT_ERR_CUDA 4        /* a CUDA runtime/driver call failed */
+#define BOKT_ERR_DEVICE 5      /* a kernel reported a timeout through the device status word */
+
+/* kernel identifiers for bokt_kernel_attrs */
+#define BOKT_KERNEL_GEMM 0
+#define BOKT_KERNEL_RMSNORM 1
+#define BOKT_KERNEL_MOE_GROUPED_GEMM 2
+
+/*
+ * Launch parameters: the CUDA counterpart of the Triton meta-parameters the
+ * reference tunes (configs/search_spaces.py:48-75).  A field left at 0 takes
+ * the kernel's default.
+ *   GEMM / grouped GEMM : block_m (128), block_n (64|128|256), block_k (64),
+ *                         stages (2..8, bounded by shared memory), group_m
+ *                         (grouped-M raster width), cta_multiplier (grouped GEMM
+ *                         persistent grid = sm_count * cta_multiplier),
+ *                         num_warps (6: TMA, MMA and four epilogue warps)
+ *   RMSNorm             : rows_per_cta, num_warps
+ */
+typedef struct bokt_params {
+  int32_t block_m;
+  int32_t block_n;
+  int32_t block_k;
+  int32_t stages;
+  int32_t group_m;
+  int32_t cta_multiplier;
+  int32_t num_warps;
+  int32_t rows_per_cta;
+  int32_t split_k;   /* reserved: must be 0 or 1 */
+  int32_t cta_group; /* reserved: must be 0 or 1 */
+  int32_t reserved[6];
+} bokt_params;
+
+typedef struct bokt_attrs {
+  int32_t shared_bytes;   /* static + dynamic shared memory per CTA */
+  int32_t registers;      /* registers per thread */
+  int32_t local_bytes;    /* local memory per thread (spill indicator) */
+  int32_t threads;        /* threads per CTA */
+  int32_t max_threads;    /* cudaFuncAttributes.maxThreadsPerBlock */
+  int32_t path;           /* 0 = tcgen05/TMA, 1 = SIMT edge path, 2 = vector, 3 = scalar */
+} bokt_attrs;
+
+/* ABI version and the sm architecture the library was built for (100). */
+int bokt_abi_version(void);
+int bokt_built_sm(void);
+
+/* Message of the last failing call on this thread ("" when none). */
+const char* bokt_last_error(void);
+
+/*
+ * C[M,N] = A[M,K] * B[K,N]; all row-major, contiguous, same element type;
+ * fp32 accumulation, result rounded to the element type on store.  Every
+ * element of C is written.  Replaces kernels/gemm.py:43-48.
+ * Shapes with K % 8, N % 8 or a pointer not 16-byte aligned take the SIMT edge
+ * path (TMA needs 16-byte row strides); everything else runs on tcgen05.
+ */
+int bokt_gemm(const void* A, const void* B, void* C, int M, int N, int K, int dtype,
+              const bokt_params* params, void* stream);
+
+/*
+ * Y[M,N] = X * rsqrt(mean(X^2, -1) + eps) * W, fp32 arithmetic, one pass over X.
+ * Replaces kernels/rmsnorm.py:29-33.
+ */
+int bokt_rmsnorm(const void* X, const void* W, void* Y, int M, int N, float eps, int dtype,
+                 const bokt_params* params, void* stream);
+
+/*
+ * For each expert e: Y[off[e]:off[e+1]] = X[off[e]:off[e+1]] * W[e], W of shape
+ * [E,K,N]; X and Y have T rows.  offsets has E+1 entries, int32
+ * (offsets_is_i64 = 0) or int64 (1), resident on the device and read by the
+ * kernel (no host copy, no per-expert launch).  Rows outside [off[0], off[E])
+ * are not written, as in the reference.  Replaces
+ * kernels/moe_grouped_gemm.py:61-65 (T is x.shape[0] there).
+ */
+int bokt_moe_grouped_gemm(const void* X, const void* W, const void* offsets, int offsets_is_i64,
+                          void* Y, int T, int E, int N, int K, int dtype, int sm_count,
+                          const bokt_params* params, void* stream);
+
+/*
+ * Routing front end for A = tokens * topk assignments given as expert ids
+ * (int32, flattened token-major, values in [0, E)).  Outputs (all int32, device):
+ *   counts[E]      tokens per expert
+ *   offsets[E+1]   exclusive prefix sum of counts (offsets[E] = A)
+ *   perm[A]        stable sort of assignments by expert: perm[j] = assignment index
+ *                  placed at packed row j
+ *   inv_perm[A]    combine index: inv_perm[i] = packed row of assignment i
+ * offsets64 (optional, may be NULL) receives the same offsets as int64.
+ * workspace: device scratch of bokt_moe_route_workspace_bytes(A, E) bytes.
+ * Ids outside [0, E) are an error: the kernel sets the device status word and
+ * the outputs are unspecified.
+ */
+int64_t bokt_moe_route_workspace_bytes(int A, int E);
+int bokt_moe_route(const int32_t* expert_ids, int A, int E, int32_t* counts, int32_t* offsets,
+                   int64_t* offsets64, int32_t* perm, int32_t* inv_perm, void* workspace,
+                   int64_t workspace_bytes, void* stream);
+
+/*
+ * Row gather: dst[j, :] = src[index[j] / divisor, :] for j < rows; row length
+ * `cols` elements of `elem_bytes` bytes; src has src_rows rows.  Packs token
+ * activations into expert order (divisor = topk, index = perm).  An index
+ * outside src sets the device status word and leaves that row unwritten.
+ */
+int bokt_gather_rows(const void* src, int64_t src_rows, void* dst, const int32_t* index, int rows,
+                     int cols, int elem_bytes, int divisor, void* stream);
+
+/* Resource usage of the kernel a call with these arguments would launch. */
+int bokt_kernel_attrs(int kernel, int dtype, int n, int k, const bokt_params* params,
+                      bokt_attrs* out);
+
+/*
+ * Device status word of the current device: 0 when no kernel has reported a
+ * bounded-wait timeout or an out-of-range routing id since the last reset.
+ * Synchronises the device.  reset != 0 clears it.
+ */
+int bokt_device_status(int* code, int* detail, int reset);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BOKT_H_ */

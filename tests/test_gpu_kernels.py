@@ -1,0 +1,267 @@
+"""GPU parity of the sm_100a kernels against the CPU oracle.
+
+Tolerance (every numeric test): the reference's FP32 gate, fp16 rtol 0.01 /
+atol 0.02 and bf16 rtol 0.02 / atol 0.15 (reference worker.py:111), plus a
+normwise relative error ||out - ref|| / ||ref|| <= 1e-2.  Outputs are
+NaN-prefilled so an unwritten element fails (reference worker.py:187).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from flashattentionanycard_b200 import _native
+from flashattentionanycard_b200.configs.search_spaces import Workload, grid_configs, search_space
+from flashattentionanycard_b200.kernels import gemm, moe_grouped_gemm, rmsnorm
+from flashattentionanycard_b200.tuner import worker
+from flashattentionanycard_b200.tuner.hardware import Hardware, prune_reason
+from oracle import numerics
+from tests.golden_cases import kernel_cases, parse_key
+from tests.gpu_helpers import as_f32, from_bits, gate, nan_like
+
+pytestmark = pytest.mark.gpu
+
+CASES = kernel_cases()
+
+
+@pytest.fixture(autouse=True)
+def clean_status(cuda_device):
+    _native.device_status(reset=True)
+    yield
+    code, detail = _native.device_status(reset=True)
+    assert code == 0, f"device status {code} (detail {detail})"
+
+
+def run_case(kernel, dtype, case, params, device, sm_count):
+    if kernel == "gemm":
+        a, b = from_bits(case["a"], dtype, device), from_bits(case["b"], dtype, device)
+        out = nan_like((a.shape[0], b.shape[1]), dtype, device)
+        gemm.launch(a, b, out, params)
+        ref = numerics.gemm_fp32(as_f32(a), as_f32(b))
+    elif kernel == "rmsnorm":
+        x, w = from_bits(case["x"], dtype, device), from_bits(case["weight"], dtype, device)
+        out = nan_like(tuple(x.shape), dtype, device)
+        rmsnorm.launch(x, w, out, params, 1e-6)
+        ref = numerics.rmsnorm_fp32(as_f32(x), as_f32(w), 1e-6)
+    else:
+        x, w = from_bits(case["x"], dtype, device), from_bits(case["weight"], dtype, device)
+        starts = case["starts"]
+        offsets = torch.tensor(starts, dtype=torch.int64, device=device)
+        out = nan_like((x.shape[0], w.shape[2]), dtype, device)
+        moe_grouped_gemm.launch(x, w, offsets, out, params, sm_count)
+        ref = numerics.grouped_gemm_fp32(as_f32(x), as_f32(w), starts)
+    torch.cuda.synchronize()
+    return out, ref
+
+
+@pytest.mark.parametrize("key", sorted(CASES))
+def test_golden_cases_all_smoke_configs(key, cuda_device):
+    """Every golden input (drawn as the reference draws) x every smoke config."""
+    kernel, dtype, _, _ = parse_key(key)
+    sm = Hardware.detect(cuda_device.index).sm_count
+    for params in grid_configs(search_space(kernel, "smoke")):
+        out, ref = run_case(kernel, dtype, CASES[key], params, cuda_device, sm)
+        gate(out, ref, dtype)
+
+
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+@pytest.mark.parametrize("kernel", ["gemm", "rmsnorm", "moe_grouped_gemm"])
+@pytest.mark.parametrize("shape", [(64, 128, 64), (37, 77, 93), (1, 1, 1)])
+def test_gpu_outputs(kernel, dtype, shape, cuda_device):
+    """The reference's own GPU test (tests/test_correctness.py:550-571) through
+    this worker's prepare/check_output."""
+    hardware = Hardware.detect(cuda_device.index)
+    m, n, k = shape
+    w = Workload(kernel, m, n, k, dtype, (0, 1, 33, 0, 9))
+    for p in grid_configs(search_space(kernel, "smoke")):
+        for seed in (0, 17):
+            call, out, reference = worker.prepare(w, cuda_device, seed, hardware.sm_count)
+            out.fill_(float("nan"))
+            call(p)
+            torch.cuda.synchronize(cuda_device)
+            worker.check_output(out, reference, dtype)
+
+
+TC_SHAPES = [(1, 8, 8), (128, 256, 64), (129, 136, 72), (300, 520, 1000), (257, 264, 4104),
+             (1000, 64, 128)]
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+@pytest.mark.parametrize("shape", TC_SHAPES)
+def test_tcgen05_gemm_edges_every_legal_config(shape, dtype, cuda_device):
+    """tcgen05 path (K, N multiples of 8): ragged M/N/K tails under every legal
+    (BLOCK_N, stages, GROUP_M) configuration of the full space."""
+    m, n, k = shape
+    g = torch.Generator().manual_seed(m * 7 + n)
+    a = torch.randn(m, k, generator=g).to(worker_dtype(dtype))
+    b = torch.randn(k, n, generator=g).to(worker_dtype(dtype))
+    ref = numerics.gemm_fp32(as_f32(a), as_f32(b))
+    a, b = a.to(cuda_device), b.to(cuda_device)
+    hw = Hardware.detect(cuda_device.index)
+    seen = 0
+    for p in grid_configs(search_space("gemm")):
+        if prune_reason(hw, "gemm", p) or (p["GROUP_M"] not in (1, 8)):
+            continue
+        out = nan_like((m, n), dtype, cuda_device)
+        compiled = gemm.launch(a, b, out, p)
+        assert compiled.path == "tcgen05"
+        torch.cuda.synchronize()
+        gate(out, ref, dtype)
+        seen += 1
+    assert seen >= 10
+
+
+def worker_dtype(dtype):
+    return {"bf16": torch.bfloat16, "fp16": torch.float16}[dtype]
+
+
+@pytest.mark.parametrize("counts", [(0, 1, 33, 0, 9), (0, 0, 0, 300), (128, 0, 129, 1, 255),
+                                    (0, 16, 64, 256, 1024, 32, 8, 128)])
+@pytest.mark.parametrize("offset_dtype", [torch.int32, torch.int64])
+def test_tcgen05_grouped_gemm_ragged_experts(counts, offset_dtype, cuda_device):
+    n, k = 264, 136
+    g = torch.Generator().manual_seed(len(counts))
+    x = torch.randn(sum(counts), k, generator=g).bfloat16()
+    w = (0.5 * torch.randn(len(counts), k, n, generator=g)).bfloat16()
+    starts = [0]
+    for c in counts:
+        starts.append(starts[-1] + c)
+    ref = numerics.grouped_gemm_fp32(as_f32(x), as_f32(w), starts)
+    xd, wd = x.to(cuda_device), w.to(cuda_device)
+    offsets = torch.tensor(starts, dtype=offset_dtype, device=cuda_device)
+    hw = Hardware.detect(cuda_device.index)
+    for p in grid_configs(search_space("moe_grouped_gemm")):
+        if prune_reason(hw, "moe_grouped_gemm", p) or p["num_stages"] not in (2, 4):
+            continue
+        out = nan_like((x.shape[0], n), "bf16", cuda_device)
+        compiled = moe_grouped_gemm.launch(xd, wd, offsets, out, p, hw.sm_count)
+        assert compiled.path == "tcgen05"
+        torch.cuda.synchronize()
+        gate(out, ref, "bf16")
+
+
+def test_grouped_gemm_leaves_rows_outside_experts(cuda_device):
+    """Rows before offsets[0] and after offsets[E] are not written (reference
+    kernel writes only [start, start + count) per expert)."""
+    n, k = 64, 64
+    x = torch.randn(40, k).bfloat16()
+    w = torch.randn(2, k, n).bfloat16()
+    starts = [5, 20, 31]
+    ref = numerics.grouped_gemm_fp32(as_f32(x), as_f32(w), starts)
+    out = nan_like((40, n), "bf16", cuda_device)
+    offsets = torch.tensor(starts, dtype=torch.int32, device=cuda_device)
+    moe_grouped_gemm.launch(x.to(cuda_device), w.to(cuda_device), offsets, out,
+                            {"BLOCK_N": 64, "num_stages": 2}, 148)
+    torch.cuda.synchronize()
+    got = out.float().cpu().numpy()
+    assert np.isnan(got[:5]).all() and np.isnan(got[31:]).all()
+    gate(out[5:31], ref[5:31], "bf16")
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+@pytest.mark.parametrize("shape", [(1, 8), (3, 4096), (37, 77), (513, 520), (64, 16384),
+                                   (7, 65536), (2, 5)])
+def test_rmsnorm_every_config(shape, dtype, cuda_device):
+    m, n = shape
+    g = torch.Generator().manual_seed(n)
+    x = torch.randn(m, n, generator=g).to(worker_dtype(dtype))
+    w = (1 + 0.1 * torch.randn(n, generator=g)).to(worker_dtype(dtype))
+    ref = numerics.rmsnorm_fp32(as_f32(x), as_f32(w), 1e-6)
+    xd, wd = x.to(cuda_device), w.to(cuda_device)
+    for p in grid_configs(search_space("rmsnorm")):
+        out = nan_like((m, n), dtype, cuda_device)
+        rmsnorm.launch(xd, wd, out, p, 1e-6)
+        torch.cuda.synchronize()
+        gate(out, ref, dtype)
+
+
+def test_unaligned_pointer_takes_edge_path(cuda_device):
+    """A view starting 2 bytes into a buffer is not 16-byte aligned: the
+    library must not hand it to TMA."""
+    base = torch.randn(1, 64 * 64 + 1).bfloat16()
+    a_cpu = base[0, 1:].reshape(64, 64)
+    b_cpu = torch.randn(64, 64).bfloat16()
+    ref = numerics.gemm_fp32(as_f32(a_cpu), as_f32(b_cpu))
+    dev = base.to(cuda_device)
+    a = dev[0, 1:].view(64, 64)
+    assert a.data_ptr() % 16 != 0
+    out = nan_like((64, 64), "bf16", cuda_device)
+    gemm.launch(a, b_cpu.to(cuda_device), out, {})
+    torch.cuda.synchronize()
+    gate(out, ref, "bf16")
+
+
+def test_launch_errors_raise(cuda_device):
+    a = torch.randn(64, 64, device=cuda_device).bfloat16()
+    out = torch.empty(64, 64, device=cuda_device).bfloat16()
+    with pytest.raises(RuntimeError, match="block_n"):
+        gemm.launch(a, a, out, {"BLOCK_N": 96})
+    with pytest.raises(RuntimeError, match="shared memory"):
+        gemm.launch(a, a, out, {"BLOCK_N": 256, "num_stages": 8})
+    with pytest.raises(ValueError):
+        gemm.launch(a, a.half(), out, {})
+    with pytest.raises(RuntimeError, match="num_warps"):
+        rmsnorm.launch(a, a[0].contiguous(), out, {"num_warps": 3})
+
+
+def test_compiled_metadata_fields(cuda_device):
+    a = torch.randn(256, 256, device=cuda_device).bfloat16()
+    out = torch.empty_like(a)
+    compiled = gemm.launch(a, a, out, {"BLOCK_N": 128, "num_stages": 4})
+    hw = Hardware.detect(cuda_device.index)
+    assert 0 < compiled.metadata.shared <= hw.shared_memory_per_block
+    assert compiled.n_regs > 0 and compiled.n_spills == 0 and compiled.threads == 192
+    c2 = rmsnorm.launch(a, a[0].contiguous(), out, {"ROWS_PER_CTA": 1, "num_warps": 4})
+    assert c2.path == "vector" and c2.n_spills == 0
+
+
+@pytest.mark.parametrize("kernel", ["gemm", "rmsnorm", "moe_grouped_gemm"])
+def test_launch_is_graph_capturable(kernel, cuda_device):
+    """No sync, allocation or host read-back inside launch: a CUDA graph of the
+    call replays to the same result (reference worker.py:148-151)."""
+    hw = Hardware.detect(cuda_device.index)
+    w = Workload(kernel, 256, 512, 384, "bf16", (100, 0, 300, 12))
+    call, out, ref = worker.prepare(w, cuda_device, 3, hw.sm_count)
+    p = next(grid_configs(search_space(kernel, "smoke")))
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        call(p)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    out.fill_(float("nan"))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        call(p)
+    graph.replay()
+    torch.cuda.synchronize()
+    worker.check_output(out, ref, "bf16")
+
+
+def test_cuda_measurement(cuda_device):
+    x = torch.ones(1024, device=cuda_device)
+    result = worker.measure(lambda: x.add_(1), worker.Measurement(2, 3, 2, 1))
+    assert len(result["samples_ms"]) == 3
+    assert result["latency_ms"] > 0
+
+
+@pytest.mark.parametrize("kernel", ["gemm", "rmsnorm", "moe_grouped_gemm"])
+@pytest.mark.parametrize("dtype", ["fp16", "bf16"])
+def test_worker_evaluate_and_confirmation(kernel, dtype, cuda_device):
+    """The full worker path: validation seeds, smem check, CUDA-graph timing,
+    and the paired candidate/torch confirmation (reference test_correctness.py:586-614)."""
+    from dataclasses import asdict
+
+    workload = Workload(kernel, 37, 77, 93, dtype, (0, 1, 33, 0, 9))
+    spec = {
+        "device": cuda_device.index,
+        "workload": asdict(workload),
+        "params": next(grid_configs(search_space(kernel, "smoke"))),
+        "measurement": asdict(worker.Measurement(2, 3, 2, 2)),
+    }
+    result = worker.evaluate(spec)
+    assert result["implementation"] == worker.CANDIDATE and len(result["validation"]) == 2
+    order = ["candidate", "torch"] if dtype == "fp16" else ["torch", "candidate"]
+    pair = worker.evaluate_confirmation(dict(spec, order=order))
+    assert pair["candidate"]["implementation"] == worker.CANDIDATE
+    assert pair["torch"]["implementation"] == worker.BASELINES[kernel]

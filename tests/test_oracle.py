@@ -1,0 +1,108 @@
+"""Pin the CPU oracle against the reference's own outputs (tests/golden) — CPU only."""
+
+import numpy as np
+import pytest
+
+from oracle import numerics, routing
+from tests.golden_cases import kernel_cases, parse_key, routing_cases
+
+KERNEL_CASES = kernel_cases()
+ROUTING_CASES = routing_cases()
+
+
+def oracle_output(kernel, dtype, case):
+    if kernel == "gemm":
+        return numerics.gemm_fp32(numerics.to_f32(case["a"], dtype), numerics.to_f32(case["b"], dtype))
+    if kernel == "rmsnorm":
+        return numerics.rmsnorm_fp32(
+            numerics.to_f32(case["x"], dtype), numerics.to_f32(case["weight"], dtype), 1e-6
+        )
+    return numerics.grouped_gemm_fp32(
+        numerics.to_f32(case["x"], dtype), numerics.to_f32(case["weight"], dtype), case["starts"]
+    )
+
+
+@pytest.mark.parametrize("key", sorted(KERNEL_CASES))
+def test_oracle_matches_reference_fp32(key):
+    """The oracle restates worker.py:64,73-74,88-90: agree with the reference's
+    own FP32 output to fp32 rounding (summation order may differ)."""
+    kernel, dtype, _, _ = parse_key(key)
+    case = KERNEL_CASES[key]
+    mine = oracle_output(kernel, dtype, case)
+    ref = case["ref"]
+    assert mine.shape == ref.shape
+    np.testing.assert_allclose(mine, ref, rtol=2e-5, atol=2e-5 * max(1.0, float(np.abs(ref).max())))
+
+
+@pytest.mark.parametrize("key", sorted(k for k, v in KERNEL_CASES.items() if "triton" in v))
+def test_reference_triton_kernel_passes_oracle_gate(key):
+    """The reference's actual Triton kernel output (CPU interpreter) passes the
+    gate against the oracle, and sits within one rounding step of it."""
+    kernel, dtype, _, _ = parse_key(key)
+    case = KERNEL_CASES[key]
+    ref = oracle_output(kernel, dtype, case)
+    out = numerics.to_f32(case["triton"], dtype)
+    stats = numerics.check_output(out, ref, dtype)
+    assert stats["normwise_rel_error"] < 1e-2
+    rounded = numerics.round_to(ref, dtype)
+    ulp = np.abs(rounded) * (2.0**-7 if dtype == "bf16" else 2.0**-10) + 1e-6
+    assert np.all(np.abs(out - rounded) <= 2 * ulp + 1e-3 * np.abs(ref).max())
+
+
+def test_gate_rejects_planted_error():
+    """A wrong answer planted in the oracle's output fails the gate."""
+    case = KERNEL_CASES["gemm|bf16|64x128x64|0"]
+    ref = oracle_output("gemm", "bf16", case)
+    bad = ref.copy()
+    bad[3, 5] += 1.0
+    with pytest.raises(AssertionError):
+        numerics.check_output(bad, ref, "bf16")
+    nan = ref.copy()
+    nan[0, 0] = np.nan
+    with pytest.raises(AssertionError):
+        numerics.check_output(nan, ref, "bf16")
+
+
+def test_bf16_conversion_matches_torch():
+    torch = pytest.importorskip("torch")
+    x = torch.randn(4096, generator=torch.Generator().manual_seed(0)) * 100
+    x[:4] = torch.tensor([0.0, -0.0, 1e-40, 3.3895e38])
+    ref_bits = x.to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    assert np.array_equal(numerics.f32_to_bf16_bits(x.numpy()), ref_bits)
+    back = x.to(torch.bfloat16).float().numpy()
+    assert np.array_equal(numerics.bf16_bits_to_f32(ref_bits), back)
+    h_bits = x.to(torch.float16).view(torch.int16).numpy().view(np.uint16)
+    assert np.array_equal(numerics.f32_to_fp16_bits(x.numpy()), h_bits)
+
+
+@pytest.mark.parametrize("key", sorted(ROUTING_CASES))
+def test_routing_oracle_matches_golden(key):
+    case = ROUTING_CASES[key]
+    experts = int(key.split("|")[2])
+    counts, offsets, perm, inv = routing.route(case["ids"], experts)
+    assert np.array_equal(counts, case["counts"])
+    assert np.array_equal(offsets, case["offsets"])
+    assert np.array_equal(perm, case["perm"])
+    assert np.array_equal(inv[perm], np.arange(perm.size))
+
+
+def test_routing_edge_cases():
+    # all assignments on one expert, empty experts at both ends
+    ids = np.full(37, 2, dtype=np.int32)
+    counts, offsets, perm, inv = routing.route(ids, 5)
+    assert counts.tolist() == [0, 0, 37, 0, 0]
+    assert offsets.tolist() == [0, 0, 0, 37, 37, 37]
+    assert perm.tolist() == list(range(37))
+    # empty input
+    counts, offsets, perm, inv = routing.route(np.zeros(0, dtype=np.int32), 3)
+    assert counts.tolist() == [0, 0, 0] and offsets.tolist() == [0, 0, 0, 0] and perm.size == 0
+    with pytest.raises(ValueError):
+        routing.route(np.array([0, 3], dtype=np.int32), 3)
+
+
+def test_grouped_oracle_leaves_uncovered_rows():
+    x = np.ones((6, 2), np.float32)
+    w = np.ones((2, 2, 3), np.float32)
+    out = numerics.grouped_gemm_fp32(x, w, [1, 3, 5])
+    assert np.isnan(out[0]).all() and np.isnan(out[5]).all()
+    assert np.all(out[1:5] == 2.0)
