@@ -82,6 +82,8 @@ SIGNATURES = {
     ),
     "bokt_moe_route_workspace_bytes": (_I64, [_I32, _I32]),
     "bokt_moe_route": (_I32, [_VP, _I32, _I32, _VP, _VP, _VP, _VP, _VP, _VP, _I64, _VP]),
+    "bokt_moe_route_noalloc_max_words": (_I64, []),
+    "bokt_moe_route_noalloc": (_I32, [_VP, _I32, _I32, _VP, _VP, _VP, _VP, _VP, _VP]),
     "bokt_gather_rows": (_I32, [_VP, _I64, _VP, _VP, _I32, _I32, _I32, _I32, _VP]),
     "bokt_kernel_attrs": (
         _I32,

@@ -515,3 +515,77 @@ int bokt_device_status(int* code, int* detail, int reset) {
 }
 
 }  // extern "C"
+
+// =================================================================== allocation-free routing
+// bokt_moe_route_noalloc: the routing front end for callers that cannot call
+// cudaMalloc (or any allocator) at all.  The per-chunk expert table that
+// bokt_moe_route keeps in a caller-provided workspace lives here in a fixed
+// device array instead, which every GPU that loads this library holds until
+// the process exits.  Host code never dereferences or passes the array's name
+// to a kernel: in host code that name is only a host-side stand-in, so the
+// device address is looked up with cudaGetSymbolAddress once per device.
+namespace {
+
+// chunks * experts int32 words, chunks = ceil(assignments / 4096).
+constexpr int64_t kRouteScratchWords = 64 * 1024;  // 256 KiB
+
+static __device__ __align__(256) int32_t g_route_scratch[kRouteScratchWords];
+
+int32_t* g_route_scratch_ptr[kMaxDevices] = {};
+std::mutex g_route_scratch_mu;
+
+// Device address of g_route_scratch on the current device, resolved on the
+// first call per device (that first call must not be inside stream capture).
+int route_scratch(int32_t** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(BOKT_ERR_UNSUPPORTED, "device index %d", dev);
+  std::lock_guard<std::mutex> lock(g_route_scratch_mu);
+  if (!g_route_scratch_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_route_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_route_scratch)");
+    g_route_scratch_ptr[dev] = static_cast<int32_t*>(p);
+  }
+  *out = g_route_scratch_ptr[dev];
+  return BOKT_OK;
+}
+
+}  // namespace
+
+extern "C" int64_t bokt_moe_route_noalloc_max_words(void) { return kRouteScratchWords; }
+
+extern "C" int bokt_moe_route_noalloc(const int32_t* expert_ids, int A, int E, int32_t* counts,
+                                      int32_t* offsets, int64_t* offsets64, int32_t* perm,
+                                      int32_t* inv_perm, void* stream) {
+  g_err[0] = 0;
+  if (A < 0 || E <= 0) return fail(BOKT_ERR_INVALID, "need A >= 0 and E > 0");
+  if (E > bokt::kRouteMaxExperts)
+    return fail(BOKT_ERR_UNSUPPORTED, "at most %d experts", bokt::kRouteMaxExperts);
+  if (!counts || !offsets || (A > 0 && (!expert_ids || !perm || !inv_perm)))
+    return fail(BOKT_ERR_INVALID, "null pointer");
+  const int64_t words = bokt_moe_route_workspace_bytes(A, E) / 4;
+  if (words > kRouteScratchWords)
+    return fail(BOKT_ERR_UNSUPPORTED,
+                "bokt_moe_route_noalloc: ceil(A/4096) * E = %lld scratch words exceeds the fixed "
+                "%lld-word device array (A=%d, E=%d); use bokt_moe_route with a workspace",
+                (long long)words, (long long)kRouteScratchWords, A, E);
+  int32_t* scratch = nullptr;
+  int rc = route_scratch(&scratch);
+  if (rc) return rc;
+  // Same kernels as bokt_moe_route.  route_count overwrites every scratch word
+  // the later launches read, so no clearing is needed between calls.
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int chunks = (A + bokt::kRouteChunk - 1) / bokt::kRouteChunk;
+  if (chunks > 0)
+    bokt::route_count_kernel<<<chunks, bokt::kRouteThreads, 0, s>>>(expert_ids, A, E, scratch);
+  bokt::route_scan_kernel<<<1, 1024, 0, s>>>(scratch, chunks, E, counts, offsets,
+                                             reinterpret_cast<long long*>(offsets64));
+  if (chunks > 0)
+    bokt::route_scatter_kernel<<<chunks, bokt::kRouteThreads, 0, s>>>(expert_ids, A, E, scratch,
+                                                                      perm, inv_perm);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "moe_route_noalloc launch");
+  return BOKT_OK;
+}

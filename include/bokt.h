@@ -143,6 +143,31 @@ int bokt_moe_route(const int32_t* expert_ids, int A, int E, int32_t* counts, int
                    int64_t workspace_bytes, void* stream);
 
 /*
+ * bokt_moe_route without a workspace argument, for callers that cannot
+ * allocate device memory at all: code running where every byte of device
+ * memory is owned by another allocator (a framework's caching pool, a
+ * serving engine's pre-partitioned arena), a foreign runtime bound through
+ * this C ABI with no device allocator of its own, or a real-time loop where
+ * cudaMalloc's implicit synchronisation is not allowed.  No counterpart in the
+ * reference (its offsets are a host prefix sum, tuner/worker.py:83-86).
+ *
+ * Scratch is a fixed 256 KiB device array inside the library (every GPU that
+ * loads the library holds it until the process exits).  Limit:
+ * ceil(A / 4096) * E <= bokt_moe_route_noalloc_max_words() (65536), e.g.
+ * 32768 assignments x 1024 experts or 1,048,576 x 256; larger requests fail
+ * with BOKT_ERR_UNSUPPORTED and a message, nothing is launched.  The first call
+ * on each device looks the array's device address up (cudaGetSymbolAddress),
+ * so make that first call outside stream capture.  All calls on a device share
+ * the one array: calls that overlap on the GPU (different streams, no ordering
+ * between them) race and give wrong results; calls in one stream are fine.
+ * Outputs are identical to bokt_moe_route's.  Allocates nothing.
+ */
+int64_t bokt_moe_route_noalloc_max_words(void);
+int bokt_moe_route_noalloc(const int32_t* expert_ids, int A, int E, int32_t* counts,
+                           int32_t* offsets, int64_t* offsets64, int32_t* perm, int32_t* inv_perm,
+                           void* stream);
+
+/*
  * Row gather: dst[j, :] = src[index[j] / divisor, :] for j < rows; row length
  * `cols` elements of `elem_bytes` bytes; src has src_rows rows.  Packs token
  * activations into expert order (divisor = topk, index = perm).  An index
