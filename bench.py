@@ -41,6 +41,8 @@ sys.path.insert(0, str(REPO))
 METRIC = "TFLOP/s (GEMM, MoE grouped GEMM) & RMSNorm GB/s vs B200 peak at 1–8 GPUs"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 L2_BYTES = 126 * 1024 * 1024
+# Rotating input sets together span 4x L2, so a set is long evicted when it is reused.
+ROTATION_BYTES = 4 * L2_BYTES
 
 
 # ----------------------------------------------------------------------------- utilities
@@ -56,14 +58,17 @@ def load_peaks():
 
 
 def profile_traffic(workload):
-    """DRAM bytes per launch of the dominant kernel from the committed ncu summary."""
+    """(DRAM bytes per launch, source) of the dominant kernel from the committed ncu summary."""
     path = REPO / "profiles" / "traffic.json"
     if not path.exists():
-        return None
+        return None, None
     try:
-        return json.loads(path.read_text()).get(workload)
+        entry = json.loads(path.read_text()).get(workload)
     except ValueError:
-        return None
+        return None, None
+    if not entry:
+        return None, None
+    return entry.get("bytes_per_launch"), entry.get("source")
 
 
 class ClockSampler:
@@ -127,23 +132,30 @@ class ClockSampler:
         }
 
 
-def kernel_durations_ms(stream, launches):
-    """Device duration of each launch in ``launches`` (callables issuing one
-    kernel each), measured with CUDA events on ``stream``.  A sleep kernel
-    queued first keeps the GPU busy while the host enqueues, so each event
-    pair brackets only its kernel."""
+def graph_time_ms(stream, fn, count, reps=3):
+    """Average device time of ``fn`` (one kernel launch) over ``count`` launches
+    captured in one CUDA graph, timed with CUDA events on ``stream``; best of
+    ``reps`` replays."""
     import torch
 
-    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-              for _ in launches]
-    with torch.cuda.stream(stream):
-        torch.cuda._sleep(int(2e6) + 200000 * len(launches))
-        for (begin, end), fn in zip(events, launches):
-            begin.record(stream)
-            fn()
-            end.record(stream)
-    stream.synchronize()
-    return [b.elapsed_time(e) for b, e in events]
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(count):
+            fn(i)
+    graph.replay()
+    torch.cuda.synchronize()
+    best = None
+    for _ in range(reps):
+        b, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        b.record(stream)
+        with torch.cuda.stream(stream):
+            graph.replay()
+        e.record(stream)
+        e.synchronize()
+        t = b.elapsed_time(e) / count
+        best = t if best is None else min(best, t)
+    del graph
+    return best
 
 
 def cpu_threads():
@@ -171,7 +183,7 @@ class Rmsnorm:
         # Rank r owns rows [r*m, (r+1)*m) of a (world*m)-row matrix: distinct seed per shard.
         x, w = workloads.rmsnorm_inputs(self.m, self.n, "bf16", seed=rank, device=device)
         per_set = 2 * x.numel() * 2
-        self.sets = max(2, math.ceil(2 * L2_BYTES / per_set))
+        self.sets = max(2, math.ceil(ROTATION_BYTES / per_set))
         self.x = [x] + [x.roll(i, 0).contiguous() for i in range(1, self.sets)]
         self.y = [torch.empty_like(x) for _ in range(self.sets)]
         self.w = w
@@ -267,7 +279,7 @@ class Gemm:
         self.n_local = n_local
         self.flops_per_step = 2.0 * size * size * n_local
         per_set = (a.numel() + b.numel() + size * n_local) * 2
-        self.sets = max(1, math.ceil(2 * L2_BYTES / per_set)) if per_set < 2 * L2_BYTES else 1
+        self.sets = max(1, math.ceil(ROTATION_BYTES / per_set)) if per_set < ROTATION_BYTES else 1
         self.A = [a] + [a.roll(i, 0).contiguous() for i in range(1, self.sets)]
         self.C = [torch.empty(size, n_local, device=device, dtype=a.dtype) for _ in range(self.sets)]
         self.split = split
@@ -350,7 +362,7 @@ class MoeSmall:
         nonempty = sum(1 for c in counts if c)
         self.bytes_per_step = (t * self.k + nonempty * self.k * self.n + t * self.n) * 2
         per_set = self.bytes_per_step
-        self.sets = max(2, math.ceil(2 * L2_BYTES / per_set))
+        self.sets = max(2, math.ceil(ROTATION_BYTES / per_set))
         self.X = [x] + [x.roll(i, 0).contiguous() for i in range(1, self.sets)]
         self.W = [w] + [w.roll(i, 1).contiguous() for i in range(1, self.sets)]
         self.Y = [torch.empty(t, self.n, device=device, dtype=x.dtype) for _ in range(self.sets)]
@@ -419,7 +431,7 @@ class MoeLarge:
         from flashattentionanycard_b200.kernels.moe_routing import MoeRouter
 
         if world > 1:
-            raise SystemExit("moe_large runs on one GPU in this build (expert parallelism pending)")
+            raise SystemExit("moe_large runs on one GPU (expert-parallel sharding is not implemented yet)")
         cfg = workloads.MOE_LARGE
         self.cfg = cfg
         self.params = default_params("moe_grouped_gemm")
@@ -710,17 +722,15 @@ def run_ours(args):
     ms_per_step = ms / steps
     value = workload.value(ms_per_step / 1e3, world)
 
-    # dominant kernel: per-launch device duration with CUDA events on its stream
+    # Dominant kernel's average launch duration.  A one-kernel step: the timed
+    # region itself (events around K launches).  Otherwise a graph of the
+    # dominant kernel alone, timed the same way.
     if workload.launches_per_step == 1:
-        launches = [(lambda i=i: workload.step(i)) for i in range(min(steps, 50))]
+        kernel_ms = ms_per_step
+        kernel_timing = "timed region / launches"
     else:
-        launches = [(lambda i=i: _last_kernel(workload, i)) for i in range(20)]
-        for i in range(3):
-            with torch.cuda.stream(stream):
-                workload.step(i)
-        stream.synchronize()
-    durations = kernel_durations_ms(stream, launches)
-    kernel_ms = statistics.median(durations)
+        kernel_ms = graph_time_ms(stream, lambda i: _last_kernel(workload, i), 20)
+        kernel_timing = "graph of 20 launches of the dominant kernel alone, best of 3"
     if workload.bound == "hbm" and workload.unit == "GB/s":
         achieved = workload.bytes_per_step / (kernel_ms / 1e3) / 1e9
         peak = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
@@ -733,11 +743,12 @@ def run_ours(args):
         achieved = workload.flops_per_step / (kernel_ms / 1e3) / 1e12
         peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
         unit_r = "TFLOP/s"
+    traffic, traffic_source = profile_traffic(workload.name)
     roofline = {"kernel": workload.kernel, "bound": "hbm" if unit_r == "GB/s" else "tensor",
                 "achieved": achieved, "peak": peak, "unit": unit_r, "frac": achieved / peak,
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json)" if peak_kind == "measured"
-                else "fallback", "kernel_ms_median": kernel_ms,
-                "traffic": profile_traffic(workload.name)}
+                else "fallback", "kernel_ms": kernel_ms, "kernel_timing": kernel_timing,
+                "traffic": traffic, "traffic_source": traffic_source}
 
     # end to end through the public API with pinned host buffers
     workload.e2e_setup()
@@ -766,10 +777,10 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, reps, elapsed, threads = cpu_measure(_cpu_only_workload(args.workload),
-                                                args.cpu_seconds)
+        cpu_workload = _cpu_only_workload(args.workload)
+        v, reps, elapsed, threads = cpu_measure(cpu_workload, args.cpu_seconds)
         cpu = {"value": v, "unit": workload.unit, "cores": threads, "kind": "port",
-               "sample": cpu_sample_description(_cpu_only_workload(args.workload)) +
+               "sample": cpu_sample_description(cpu_workload) +
                f"; {reps} reps in {elapsed:.1f} s"}
 
     if world > 1:
@@ -782,7 +793,7 @@ def run_ours(args):
         "metric": METRIC, "value": value, "unit": workload.unit, "n_gpus": world,
         "steps": steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
         "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
-        "dtype": workload.dtype, "data": "synthetic (seeded, BASELINE config shapes)",
+        "dtype": workload.dtype, "data": "synthetic (seeded inputs of the benchmark configuration shapes)",
         "config": workload.config(world), "roofline": roofline, "cpu_baseline": cpu,
         "e2e": e2e, "clocks": clocks, "gpu_launches": steps * workload.launches_per_step,
         "impl": "ours",
@@ -791,7 +802,7 @@ def run_ours(args):
     return 0
 
 
-def _last_kernel(workload, i):
+def _last_kernel(workload, i):  # noqa: ARG001 - same inputs every launch
     from flashattentionanycard_b200.kernels import moe_grouped_gemm
 
     moe_grouped_gemm.launch(workload.packed, workload.w, workload.router.offsets, workload.y,

@@ -37,6 +37,48 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 int param_or(int v, int dflt) { return v > 0 ? v : dflt; }
 
+// Programmatic dependent launch for every kernel (each kernel waits with
+// griddepcontrol.wait before touching global memory).  BOKT_DISABLE_PDL=1
+// turns the attribute off, e.g. to compare timings.
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("BOKT_DISABLE_PDL");
+    return !(v && v[0] && v[0] != '0');
+  }();
+  return on;
+}
+
+cudaLaunchConfig_t launch_config(dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                                 cudaLaunchAttribute* attr) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cfg;
+}
+
+// Typed launch: kernel<<<grid, block, smem, s>>>(args...) with PDL.
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                   Args... args) {
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = launch_config(grid, block, smem, s, attr);
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// Untyped launch through a kernel pointer and an argument array, with PDL.
+cudaError_t launch_ptr(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                       void** args) {
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = launch_config(grid, block, smem, s, attr);
+  return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
 // ----------------------------------------------------------------- device info
 struct DeviceInfo {
   int sm_count = 0;
@@ -196,7 +238,7 @@ int launch_tc(bool grouped, int dtype, const TcConfig& cfg, const CUtensorMap& m
   if (rc) return rc;
   void* kargs[] = {const_cast<CUtensorMap*>(&ma), const_cast<CUtensorMap*>(&mb),
                    const_cast<GemmTcArgs*>(&args)};
-  cudaError_t e = cudaLaunchKernel(fn, dim3(grid), dim3(bokt::kGemmThreads), kargs, cfg.smem, s);
+  cudaError_t e = launch_ptr(fn, dim3(grid), dim3(bokt::kGemmThreads), cfg.smem, s, kargs);
   if (e != cudaSuccess) return cuda_fail(e, "gemm_tc launch");
   return BOKT_OK;
 }
@@ -205,10 +247,9 @@ template <typename T>
 int launch_simt(const void* A, const void* B, void* C, int rows, int N, int K,
                 const void* offsets, int offsets_i64, int experts, cudaStream_t s) {
   dim3 grid((N + bokt::kSimtCols - 1) / bokt::kSimtCols, rows < 65535 ? rows : 65535);
-  bokt::gemm_simt_kernel<T><<<grid, bokt::kSimtCols, 0, s>>>(
-      static_cast<const T*>(A), static_cast<const T*>(B), static_cast<T*>(C), rows, N, K, offsets,
-      offsets_i64, experts);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch(bokt::gemm_simt_kernel<T>, grid, dim3(bokt::kSimtCols), 0, s,
+                         static_cast<const T*>(A), static_cast<const T*>(B), static_cast<T*>(C),
+                         rows, N, K, offsets, offsets_i64, experts);
   if (e != cudaSuccess) return cuda_fail(e, "gemm_simt launch");
   return BOKT_OK;
 }
@@ -245,6 +286,25 @@ int resolve_norm_config(const bokt_params* p, int N, bool vec_ok, NormConfig* ou
     if (v <= 16) vpt = v;
   }
   *out = {rows, threads, lg, vpt};
+  return BOKT_OK;
+}
+
+// The three routing launches, scratch = ceil(A / 4096) * E int32 words.
+int launch_route(const int32_t* ids, int A, int E, int32_t* scratch, int32_t* counts,
+                 int32_t* offsets, int64_t* offsets64, int32_t* perm, int32_t* inv_perm,
+                 cudaStream_t s, const char* what) {
+  const int chunks = (A + bokt::kRouteChunk - 1) / bokt::kRouteChunk;
+  cudaError_t e = cudaSuccess;
+  if (chunks > 0)
+    e = launch(bokt::route_count_kernel, dim3(chunks), dim3(bokt::kRouteThreads), 0, s, ids, A, E,
+               scratch);
+  if (e == cudaSuccess)
+    e = launch(bokt::route_scan_kernel, dim3(1), dim3(1024), 0, s, scratch, chunks, E, counts,
+               offsets, reinterpret_cast<long long*>(offsets64));
+  if (e == cudaSuccess && chunks > 0)
+    e = launch(bokt::route_scatter_kernel, dim3(chunks), dim3(bokt::kRouteThreads), 0, s, ids, A,
+               E, static_cast<const int32_t*>(scratch), perm, inv_perm);
+  if (e != cudaSuccess) return cuda_fail(e, what);
   return BOKT_OK;
 }
 
@@ -386,7 +446,7 @@ int bokt_rmsnorm(const void* X, const void* W, void* Y, int M, int N, float eps,
                                       : norm_kernel<__half>(cfg.vpt);
   void* kargs[] = {const_cast<void**>(&X), const_cast<void**>(&W), &Y, &M, &N, &eps,
                    &cfg.rows_per_cta, &cfg.tpr_log2};
-  cudaError_t e = cudaLaunchKernel(fn, dim3(grid), dim3(cfg.threads), kargs, 0, s);
+  cudaError_t e = launch_ptr(fn, dim3(grid), dim3(cfg.threads), 0, s, kargs);
   if (e != cudaSuccess) return cuda_fail(e, "rmsnorm launch");
   return BOKT_OK;
 }
@@ -410,18 +470,9 @@ int bokt_moe_route(const int32_t* expert_ids, int A, int E, int32_t* counts, int
     return fail(BOKT_ERR_INVALID, "workspace too small: need %lld bytes",
                 (long long)bokt_moe_route_workspace_bytes(A, E));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int chunks = (A + bokt::kRouteChunk - 1) / bokt::kRouteChunk;
   int32_t* ws = static_cast<int32_t*>(workspace);
-  if (chunks > 0)
-    bokt::route_count_kernel<<<chunks, bokt::kRouteThreads, 0, s>>>(expert_ids, A, E, ws);
-  bokt::route_scan_kernel<<<1, 1024, 0, s>>>(ws, chunks, E, counts, offsets,
-                                             reinterpret_cast<long long*>(offsets64));
-  if (chunks > 0)
-    bokt::route_scatter_kernel<<<chunks, bokt::kRouteThreads, 0, s>>>(expert_ids, A, E, ws, perm,
-                                                                      inv_perm);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "moe_route launch");
-  return BOKT_OK;
+  return launch_route(expert_ids, A, E, ws, counts, offsets, offsets64, perm, inv_perm, s,
+                      "moe_route launch");
 }
 
 int bokt_gather_rows(const void* src, int64_t src_rows, void* dst, const int32_t* index, int rows,
@@ -434,17 +485,17 @@ int bokt_gather_rows(const void* src, int64_t src_rows, void* dst, const int32_t
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const long long row_bytes = (long long)cols * elem_bytes;
   const int grid = rows < 65535 * 4 ? rows : 65535 * 4;
+  cudaError_t e;
   if (row_bytes % 16 == 0 && aligned16(src) && aligned16(dst)) {
     const int vecs = int(row_bytes / 16);
-    bokt::gather_rows_kernel<uint4><<<grid, 128, 0, s>>>(
-        static_cast<const uint4*>(src), src_rows, static_cast<uint4*>(dst), index, rows, vecs,
-        divisor);
+    e = launch(bokt::gather_rows_kernel<uint4>, dim3(grid), dim3(128), 0, s,
+               static_cast<const uint4*>(src), (long long)src_rows, static_cast<uint4*>(dst), index,
+               rows, vecs, divisor);
   } else {
-    bokt::gather_rows_kernel<uint8_t><<<grid, 128, 0, s>>>(
-        static_cast<const uint8_t*>(src), src_rows, static_cast<uint8_t*>(dst), index, rows,
-        int(row_bytes), divisor);
+    e = launch(bokt::gather_rows_kernel<uint8_t>, dim3(grid), dim3(128), 0, s,
+               static_cast<const uint8_t*>(src), (long long)src_rows, static_cast<uint8_t*>(dst),
+               index, rows, int(row_bytes), divisor);
   }
-  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "gather_rows launch");
   return BOKT_OK;
 }
@@ -577,15 +628,6 @@ extern "C" int bokt_moe_route_noalloc(const int32_t* expert_ids, int A, int E, i
   // Same kernels as bokt_moe_route.  route_count overwrites every scratch word
   // the later launches read, so no clearing is needed between calls.
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int chunks = (A + bokt::kRouteChunk - 1) / bokt::kRouteChunk;
-  if (chunks > 0)
-    bokt::route_count_kernel<<<chunks, bokt::kRouteThreads, 0, s>>>(expert_ids, A, E, scratch);
-  bokt::route_scan_kernel<<<1, 1024, 0, s>>>(scratch, chunks, E, counts, offsets,
-                                             reinterpret_cast<long long*>(offsets64));
-  if (chunks > 0)
-    bokt::route_scatter_kernel<<<chunks, bokt::kRouteThreads, 0, s>>>(expert_ids, A, E, scratch,
-                                                                      perm, inv_perm);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "moe_route_noalloc launch");
-  return BOKT_OK;
+  return launch_route(expert_ids, A, E, scratch, counts, offsets, offsets64, perm, inv_perm, s,
+                      "moe_route_noalloc launch");
 }

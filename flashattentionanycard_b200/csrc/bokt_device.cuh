@@ -38,6 +38,18 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+// Programmatic dependent launch.  Every kernel of the library is launched with
+// programmatic stream serialization, so it may start while the previous
+// kernel in the stream drains.  pdl_wait() blocks until that kernel has
+// completed and its memory is visible: every kernel calls it before its first
+// global-memory access.  pdl_allow_next() lets the next kernel begin its own
+// launch early.  Both are no-ops when the kernel was launched without PDL.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+__device__ __forceinline__ void pdl_allow_next() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -24,6 +24,8 @@ __global__ void __launch_bounds__(kSimtCols) gemm_simt_kernel(const T* __restric
                                                                int K, const void* offsets,
                                                                int offsets_i64, int experts) {
   __shared__ float a_row[kSimtKChunk];
+  pdl_allow_next();
+  pdl_wait();
   const int col = blockIdx.x * kSimtCols + threadIdx.x;
   for (int row = blockIdx.y; row < rows; row += gridDim.y) {
     const T* Bp = B;

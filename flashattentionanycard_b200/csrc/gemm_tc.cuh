@@ -158,6 +158,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tmem_alloc(tmem_holder, Shape::kTmemCols);
     tmem_relinquish();
   }
+  // Prologue above overlaps the previous kernel; global memory only after this.
+  pdl_allow_next();
+  pdl_wait();
 
   int ntiles;
   if constexpr (GROUPED) {

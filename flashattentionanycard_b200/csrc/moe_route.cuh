@@ -35,6 +35,8 @@ __global__ void __launch_bounds__(kRouteThreads) route_count_kernel(const int32_
                                                                      int A, int E,
                                                                      int32_t* __restrict__ chunk_counts) {
   __shared__ int hist[kRouteMaxExperts];
+  pdl_allow_next();
+  pdl_wait();
   for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
   __syncthreads();
   const int begin = blockIdx.x * kRouteChunk;
@@ -59,6 +61,8 @@ __global__ void __launch_bounds__(1024) route_scan_kernel(int32_t* __restrict__ 
   __shared__ int totals[kRouteMaxExperts];
   __shared__ int warp_sums[32];
   __shared__ int carry;
+  pdl_allow_next();
+  pdl_wait();
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     int run = 0;
     for (int c = 0; c < chunks; ++c) {
@@ -117,6 +121,8 @@ __global__ void __launch_bounds__(kRouteThreads) route_scatter_kernel(
     int32_t* __restrict__ perm, int32_t* __restrict__ inv_perm) {
   __shared__ int running[kRouteMaxExperts];
   __shared__ int wcnt[kRouteWarps][kRouteMaxExperts];
+  pdl_allow_next();
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     running[e] = chunk_base[static_cast<size_t>(blockIdx.x) * E + e];
@@ -160,6 +166,8 @@ template <typename V>
 __global__ void gather_rows_kernel(const V* __restrict__ src, long long src_rows, V* __restrict__ dst,
                                    const int32_t* __restrict__ index, int rows, int row_vecs,
                                    int divisor) {
+  pdl_allow_next();
+  pdl_wait();
   for (int j = blockIdx.x; j < rows; j += gridDim.x) {
     const int raw = index[j];
     const long long s = raw / divisor;

@@ -41,6 +41,8 @@ __global__ void rmsnorm_vec_kernel(const T* __restrict__ X, const T* __restrict_
                                    T* __restrict__ Y, int M, int N, float eps, int rows_per_cta,
                                    int tpr_log2) {
   __shared__ float red[32];
+  pdl_allow_next();
+  pdl_wait();
   const int tpr = 1 << tpr_log2;
   const int slot = threadIdx.x >> tpr_log2;
   const int tid = threadIdx.x & (tpr - 1);
@@ -97,6 +99,8 @@ __global__ void rmsnorm_generic_kernel(const T* __restrict__ X, const T* __restr
                                        T* __restrict__ Y, int M, int N, float eps,
                                        int rows_per_cta, int tpr_log2) {
   __shared__ float red[32];
+  pdl_allow_next();
+  pdl_wait();
   const int tpr = 1 << tpr_log2;
   const int slot = threadIdx.x >> tpr_log2;
   const int tid = threadIdx.x & (tpr - 1);

@@ -91,7 +91,7 @@ def main(reference_root):
             for shape, seeds in (((64, 128, 64), (0,)), ((37, 77, 93), (0, 17)), ((1, 1, 1), (0, 17))):
                 for seed in seeds:
                     record(kernel, dtype, shape, seed)
-    # BASELINE smoke GEMM shape (127 x 193 x 257, bf16, seed 0), reference N(0,1) draw.
+    # The 127 x 193 x 257 bf16 smoke GEMM shape, seed 0, reference N(0,1) draw.
     record("gemm", "bf16", (127, 193, 257), 0)
     # Grouped GEMM with the reference smoke suite's expert counts (runpod/configs/smoke.json).
     record("moe_grouped_gemm", "fp16", (1, 64, 32), 0, (0, 1, 17, 65))
