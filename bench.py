@@ -430,24 +430,55 @@ class MoeLarge:
         from flashattentionanycard_b200.configs.search_spaces import default_params
         from flashattentionanycard_b200.kernels.moe_routing import MoeRouter
 
-        if world > 1:
-            raise SystemExit("moe_large runs on one GPU (expert-parallel sharding is not implemented yet)")
         cfg = workloads.MOE_LARGE
         self.cfg = cfg
+        self.world, self.rank = world, rank
         self.params = default_params("moe_grouped_gemm")
         self.x, self.w, ids = workloads.moe_large_inputs("bf16", seed=0, device=device)
+        self.sm = torch.cuda.get_device_properties(device).multi_processor_count
+        a = ids.numel()
+        self.flops_per_step = 2.0 * a * cfg["k"] * cfg["n"]  # whole job, all ranks
+        if world > 1:
+            self._init_expert_parallel(ids, device)
+            return
         self.ids = ids.reshape(-1).to(device)
-        a = self.ids.numel()
         self.router = MoeRouter(a, cfg["experts"], device)
         self.packed = torch.empty(a, cfg["k"], device=device, dtype=torch.bfloat16)
         self.y = torch.empty(a, cfg["n"], device=device, dtype=torch.bfloat16)
-        self.flops_per_step = 2.0 * a * cfg["k"] * cfg["n"]
-        self.sm = torch.cuda.get_device_properties(device).multi_processor_count
+
+    def _init_expert_parallel(self, ids, device):
+        import numpy as np
+        import torch.distributed as dist
+
+        from flashattentionanycard_b200 import expert_parallel as ep
+
+        cfg, world, rank = self.cfg, self.world, self.rank
+        flat = ids.reshape(-1).numpy()
+        tpr = cfg["tokens"] // world
+        self.placement = ep.plan_placement(np.bincount(flat, minlength=cfg["experts"]), world)
+        self.plan = ep.plan_splits(flat, self.placement, cfg["topk"], tpr)
+        local = self.w[ep.local_weight_slices(self.placement, rank)].contiguous()
+        del self.w  # each rank keeps only its virtual experts' weights
+        self.x_local = self.x[rank * tpr:(rank + 1) * tpr].contiguous()
+        del self.x
+        self.ids_local = ids.reshape(-1)[rank * tpr * cfg["topk"]:(rank + 1) * tpr * cfg["topk"]]
+        self.ids_local = self.ids_local.to(torch_int32()).to(device)
+        self.ep = ep.ExpertParallelMoE(local, self.placement, self.plan, rank, world,
+                                       cfg["topk"], tpr, group=dist.group.WORLD,
+                                       params=self.params, sm_count=self.sm)
+        import torch
+
+        torch.cuda.empty_cache()
+        self.launches_per_step = 21  # 16 routing/keys/sorts/checks + 4 gathers + grouped GEMM
+        self.graphable = False  # NCCL all-to-all with plan split sizes: timed eagerly
 
     def step(self, i):
         from flashattentionanycard_b200.kernels import moe_grouped_gemm
         from flashattentionanycard_b200.kernels.moe_routing import gather_rows
 
+        if self.world > 1:
+            self.ep.forward(self.x_local, self.ids_local)
+            return
         self.router(self.ids)
         gather_rows(self.x, self.router.perm, self.packed, divisor=self.cfg["topk"])
         moe_grouped_gemm.launch(self.packed, self.w, self.router.offsets, self.y, self.params,
@@ -455,17 +486,36 @@ class MoeLarge:
 
     def config(self, world):
         c = self.cfg
-        return {"workload": f"moe_bf16_E{c['experts']}_K{c['k']}_N{c['n']}_T{c['tokens']}_top2_zipf1.1",
-                "partition": "single GPU (all experts local)",
-                "step": "route + gather + grouped GEMM", "l2": "W 7.5 GB > L2",
-                "params": self.params}
+        out = {"workload": f"moe_bf16_E{c['experts']}_K{c['k']}_N{c['n']}_T{c['tokens']}_top2_zipf1.1",
+               "partition": "single GPU (all experts local)",
+               "step": "route + gather + grouped GEMM", "l2": "W 7.5 GB > L2",
+               "params": self.params}
+        if world > 1:
+            p = self.placement
+            out.update({
+                "partition": f"expert-parallel over {world} GPUs: {p.virtual_experts} virtual "
+                             f"experts (hot experts replicated, rows split), LPT placement",
+                "step": "all-gather ids + route + dispatch all-to-all + grouped GEMM + "
+                        "combine all-to-all (NCCL), eager",
+                "rows_per_rank": [int(v) for v in p.rank_rows],
+                "max_replicas": int(p.replicas.max()),
+            })
+        return out
 
     def value(self, seconds_per_step, world):
-        return self.flops_per_step * world / seconds_per_step / 1e12
+        return self.flops_per_step / seconds_per_step / 1e12  # whole job at any world size
 
     def e2e_setup(self):
         import torch
 
+        if self.world > 1:
+            self.hx = self.x_local.cpu().pin_memory()
+            self.hids = self.ids_local.cpu().pin_memory()
+            self.hy = torch.empty(self.ep.out.shape, dtype=self.ep.out.dtype).pin_memory()
+            self.dx, self.dids = torch.empty_like(self.x_local), torch.empty_like(self.ids_local)
+            self.h2d = self.hx.numel() * 2 + self.hids.numel() * 4
+            self.d2h = self.hy.numel() * 2
+            return
         self.hx = self.x.cpu().pin_memory()
         self.hids = self.ids.cpu().pin_memory()
         self.hy = torch.empty(self.y.shape, dtype=self.y.dtype).pin_memory()
@@ -479,6 +529,10 @@ class MoeLarge:
 
         self.dx.copy_(self.hx, non_blocking=True)
         self.dids.copy_(self.hids, non_blocking=True)
+        if self.world > 1:
+            out = self.ep.forward(self.dx, self.dids)
+            self.hy.copy_(out, non_blocking=True)
+            return
         self.router(self.dids)
         gather_rows(self.dx, self.router.perm, self.packed, divisor=self.cfg["topk"])
         moe_grouped_gemm.launch(self.packed, self.w, self.router.offsets, self.y, self.params,
@@ -681,16 +735,18 @@ def run_ours(args):
     _native.device_status(reset=True)
 
     steps = args.steps
-    chunk = max(1, min(steps, 250))
+    graphable = getattr(workload, "graphable", True)
     graphs = []
-    done = 0
-    while done < steps:
-        count = min(chunk, steps - done)
-        graphs.append(capture_steps(workload, stream, done, count))
-        done += count
-    # one untimed replay of the first graph (graph upload)
-    graphs[0].replay()
-    torch.cuda.synchronize()
+    if graphable:
+        chunk = max(1, min(steps, 250))
+        done = 0
+        while done < steps:
+            count = min(chunk, steps - done)
+            graphs.append(capture_steps(workload, stream, done, count))
+            done += count
+        # one untimed replay of the first graph (graph upload)
+        graphs[0].replay()
+        torch.cuda.synchronize()
 
     sampler = ClockSampler(local)
     sampler.start()
@@ -702,8 +758,12 @@ def run_ours(args):
     t0 = time.perf_counter()
     begin.record(stream)
     with torch.cuda.stream(stream):
-        for g in graphs:
-            g.replay()
+        if graphable:
+            for g in graphs:
+                g.replay()
+        else:
+            for i in range(steps):
+                workload.step(i)
     end.record(stream)
     torch.cuda.synchronize()
     t1 = time.perf_counter()
@@ -802,8 +862,18 @@ def run_ours(args):
     return 0
 
 
+def torch_int32():
+    import torch
+
+    return torch.int32
+
+
 def _last_kernel(workload, i):  # noqa: ARG001 - same inputs every launch
     from flashattentionanycard_b200.kernels import moe_grouped_gemm
+
+    if getattr(workload, "world", 1) > 1:
+        workload.ep.compute()
+        return
 
     moe_grouped_gemm.launch(workload.packed, workload.w, workload.router.offsets, workload.y,
                             workload.params, workload.sm)

@@ -85,6 +85,10 @@ SIGNATURES = {
     "bokt_moe_route_noalloc_max_words": (_I64, []),
     "bokt_moe_route_noalloc": (_I32, [_VP, _I32, _I32, _VP, _VP, _VP, _VP, _VP, _VP]),
     "bokt_gather_rows": (_I32, [_VP, _I64, _VP, _VP, _I32, _I32, _I32, _I32, _VP]),
+    "bokt_gather_rows_indirect": (
+        _I32, [_VP, _I64, _VP, _VP, _I64, _VP, _I32, _I32, _I32, _I32, _I64, _VP]),
+    "bokt_ep_keys": (_I32, [_VP] * 8 + [_I32] * 7 + [_VP] * 4),
+    "bokt_check_counts": (_I32, [_VP, _VP, _I32, _I32, _VP]),
     "bokt_kernel_attrs": (
         _I32,
         [_I32, _I32, _I32, _I32, _PP, ctypes.POINTER(BoktAttrs)],

@@ -500,6 +500,67 @@ int bokt_gather_rows(const void* src, int64_t src_rows, void* dst, const int32_t
   return BOKT_OK;
 }
 
+int bokt_gather_rows_indirect(const void* src, int64_t src_rows, void* dst, const int32_t* inner,
+                               int64_t inner_len, const int32_t* outer, int rows, int cols,
+                               int elem_bytes, int divisor, int64_t base, void* stream) {
+  g_err[0] = 0;
+  if (rows < 0 || cols < 0 || src_rows < 0 || divisor <= 0 || elem_bytes <= 0 || inner_len < 0)
+    return fail(BOKT_ERR_INVALID, "bad size");
+  if (rows == 0 || cols == 0) return BOKT_OK;
+  if (!src || !dst || !inner) return fail(BOKT_ERR_INVALID, "null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const long long row_bytes = (long long)cols * elem_bytes;
+  const int grid = rows < 65535 * 4 ? rows : 65535 * 4;
+  cudaError_t e;
+  if (row_bytes % 16 == 0 && aligned16(src) && aligned16(dst)) {
+    e = launch(bokt::gather_rows_indirect_kernel<uint4>, dim3(grid), dim3(128), 0, s,
+               static_cast<const uint4*>(src), (long long)src_rows, static_cast<uint4*>(dst),
+               inner, outer, (long long)inner_len, rows, int(row_bytes / 16), divisor,
+               (long long)base);
+  } else {
+    e = launch(bokt::gather_rows_indirect_kernel<uint8_t>, dim3(grid), dim3(128), 0, s,
+               static_cast<const uint8_t*>(src), (long long)src_rows, static_cast<uint8_t*>(dst),
+               inner, outer, (long long)inner_len, rows, int(row_bytes), divisor,
+               (long long)base);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "gather_rows_indirect launch");
+  return BOKT_OK;
+}
+
+int bokt_ep_keys(const int32_t* perm, const int32_t* ids, const int32_t* offsets,
+                 const int32_t* counts, const int32_t* replicas, const int32_t* vbase,
+                 const int32_t* v_rank, const int32_t* v_local, int A, int E, int topk,
+                 int tokens_per_rank, int me, int world, int n_local, int32_t* key_send,
+                 int32_t* key_recv, int32_t* key_local, void* stream) {
+  g_err[0] = 0;
+  if (A < 0 || E <= 0 || topk <= 0 || tokens_per_rank <= 0 || world <= 0 || me < 0 ||
+      me >= world || n_local < 0)
+    return fail(BOKT_ERR_INVALID, "bad size");
+  if (A == 0) return BOKT_OK;
+  if (!perm || !ids || !offsets || !counts || !replicas || !vbase || !v_rank || !v_local ||
+      !key_send || !key_recv || !key_local)
+    return fail(BOKT_ERR_INVALID, "null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int grid = (A + 255) / 256 < 4096 ? (A + 255) / 256 : 4096;
+  cudaError_t e = launch(bokt::ep_keys_kernel, dim3(grid), dim3(256), 0, s, perm, ids, offsets,
+                         counts, replicas, vbase, v_rank, v_local, A, E, topk, tokens_per_rank,
+                         me, world, n_local, key_send, key_recv, key_local);
+  if (e != cudaSuccess) return cuda_fail(e, "ep_keys launch");
+  return BOKT_OK;
+}
+
+int bokt_check_counts(const int32_t* counts, const int32_t* expected, int n, int tag,
+                      void* stream) {
+  g_err[0] = 0;
+  if (n < 0) return fail(BOKT_ERR_INVALID, "bad size");
+  if (n == 0) return BOKT_OK;
+  if (!counts || !expected) return fail(BOKT_ERR_INVALID, "null pointer");
+  cudaError_t e = launch(bokt::check_counts_kernel, dim3(1), dim3(256), 0,
+                         static_cast<cudaStream_t>(stream), counts, expected, n, tag);
+  if (e != cudaSuccess) return cuda_fail(e, "check_counts launch");
+  return BOKT_OK;
+}
+
 int bokt_kernel_attrs(int kernel, int dtype, int n, int k, const bokt_params* params,
                       bokt_attrs* out) {
   g_err[0] = 0;

@@ -1,5 +1,5 @@
 // Device-side helpers for the sm_100a kernels: mbarriers with bounded waits,
-// TMA tile loads (no cluster multicast anywhere), tcgen05 MMA / TMEM access and
+// per-CTA TMA tile loads, tcgen05 MMA / TMEM access and
 // the shared-memory matrix descriptors.  Written from the PTX ISA (tcgen05,
 // cp.async.bulk.tensor, mbarrier chapters).
 #pragma once

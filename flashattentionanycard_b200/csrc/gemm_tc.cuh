@@ -14,7 +14,7 @@
 // Two TMEM accumulators (2 x BN fp32 columns) let the epilogue of tile i
 // overlap the main loop of tile i+1.  Operand tiles use the 128-byte swizzle:
 // A tile = 128 rows x 64 K (16 KB), B tile = 64 K rows x BN (BN/64 boxes of
-// 64 x 64).  No cluster launch and no multicast.
+// 64 x 64).  No cluster launch; every CTA loads its own tiles.
 #pragma once
 
 #include "bokt_device.cuh"

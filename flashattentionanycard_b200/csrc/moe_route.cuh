@@ -182,3 +182,91 @@ __global__ void gather_rows_kernel(const V* __restrict__ src, long long src_rows
 }
 
 }  // namespace bokt
+
+namespace bokt {
+
+constexpr int kStatusPlanMismatch = 3;
+
+// dst[j, :] = src[inner[outer ? outer[j] : j] / divisor - base, :]: the
+// two-level row gathers of expert-parallel dispatch and combine (compose a
+// routing permutation with a per-rank order without materialising the
+// composed index).  Rows whose source falls outside src are reported and
+// left unwritten.
+template <typename V>
+__global__ void gather_rows_indirect_kernel(const V* __restrict__ src, long long src_rows,
+                                            V* __restrict__ dst,
+                                            const int32_t* __restrict__ inner,
+                                            const int32_t* __restrict__ outer, long long inner_len,
+                                            int rows, int row_vecs, int divisor, long long base) {
+  pdl_allow_next();
+  pdl_wait();
+  for (int j = blockIdx.x; j < rows; j += gridDim.x) {
+    const long long o = outer ? static_cast<long long>(outer[j]) : j;
+    if (o < 0 || o >= inner_len) {
+      if (threadIdx.x == 0) report_status(kStatusBadExpertId, j);
+      continue;
+    }
+    const long long raw = inner[o];
+    const long long s = (raw < 0 ? -1 : raw / divisor) - base;
+    if (raw < 0 || s < 0 || s >= src_rows) {
+      if (threadIdx.x == 0) report_status(kStatusBadExpertId, j);
+      continue;
+    }
+    const V* sr = src + s * row_vecs;
+    V* dr = dst + static_cast<long long>(j) * row_vecs;
+    for (int c = threadIdx.x; c < row_vecs; c += blockDim.x) dr[c] = sr[c];
+  }
+}
+
+// Expert-parallel keys of every packed row p of the global routing (one rank's view).
+//   a = perm[p] (assignment, token-major), e = ids[a], q = p - offsets[e],
+//   replica j = q * R_e / c_e, virtual expert v = vbase[e] + j, dest d = v_rank[v],
+//   owner o = (a / topk) / tokens_per_rank.
+//   key_send[p]  = o == me ? d : world          (stable sort -> send order by destination)
+//   key_recv[p]  = d == me ? o : world          (-> receive order by source)
+//   key_local[p] = d == me ? v_local[v] : n_local (-> local grouped-GEMM order and offsets)
+__global__ void ep_keys_kernel(const int32_t* __restrict__ perm, const int32_t* __restrict__ ids,
+                               const int32_t* __restrict__ offsets,
+                               const int32_t* __restrict__ counts,
+                               const int32_t* __restrict__ replicas,
+                               const int32_t* __restrict__ vbase,
+                               const int32_t* __restrict__ v_rank,
+                               const int32_t* __restrict__ v_local, int A, int E, int topk,
+                               int tokens_per_rank, int me, int world, int n_local,
+                               int32_t* __restrict__ key_send, int32_t* __restrict__ key_recv,
+                               int32_t* __restrict__ key_local) {
+  pdl_allow_next();
+  pdl_wait();
+  for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < A; p += gridDim.x * blockDim.x) {
+    const int a = perm[p];
+    const int e = (a >= 0 && a < A) ? ids[a] : -1;
+    if (e < 0 || e >= E) {
+      report_status(kStatusBadExpertId, p);
+      key_send[p] = world;
+      key_recv[p] = world;
+      key_local[p] = n_local;
+      continue;
+    }
+    const long long q = p - offsets[e];
+    const int c = counts[e];
+    const int j = c > 0 ? static_cast<int>((q * replicas[e]) / c) : 0;
+    const int v = vbase[e] + j;
+    const int d = v_rank[v];
+    const int o = (a / topk) / tokens_per_rank;
+    key_send[p] = o == me ? d : world;
+    key_recv[p] = d == me ? o : world;
+    key_local[p] = d == me ? v_local[v] : n_local;
+  }
+}
+
+// Flags kStatusPlanMismatch when counts[0..n) differs from the planned sizes
+// (the NCCL split sizes were fixed when the plan was made).
+__global__ void check_counts_kernel(const int32_t* __restrict__ counts,
+                                    const int32_t* __restrict__ expected, int n, int tag) {
+  pdl_allow_next();
+  pdl_wait();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    if (counts[i] != expected[i]) report_status(kStatusPlanMismatch, tag * 65536 + i);
+}
+
+}  // namespace bokt

@@ -1,0 +1,315 @@
+"""Expert-parallel MoE grouped GEMM across GPUs (one process per GPU, NCCL).
+
+The reference runs one GPU only; this is the multi-GPU form of its grouped GEMM
+(``kernels/moe_grouped_gemm.py``) for the 64-expert, top-2, Zipf-routed case.
+
+Layout: tokens are owned in contiguous blocks of ``tokens_per_rank`` per rank
+(rank r owns tokens [r*T/G, (r+1)*T/G)).  Experts are served by *virtual
+experts*: expert e gets ``replicas[e]`` of them, which split the expert's packed
+rows contiguously (packed row q of the expert goes to replica q*R_e // c_e), so
+a hot expert is spread over several GPUs without splitting any row or column;
+every assignment row crosses NVLink once on dispatch and once on combine.
+Virtual experts are packed onto ranks with longest-processing-time-first.  The
+placement is a deterministic function of the global expert counts, so every
+rank derives the same plan and the result is bit-identical to the one-GPU
+routing.
+
+One step (every rank, same order of collectives):
+  1. all-gather the int32 expert ids of all tokens (NCCL, 4 * T * topk bytes);
+  2. global routing on every rank (bokt_moe_route): counts, offsets, perm;
+  3. per-row keys (bokt_ep_keys) and three stable counting sorts: the send
+     order (by destination), the receive order (by source) and the local
+     grouped-GEMM order (by local virtual expert, which also gives its offsets);
+  4. the sort sizes are checked against the plan on the device
+     (bokt_check_counts); the NCCL split sizes come from the plan, so the step
+     needs no host synchronisation;
+  5. gather the rows to send (bokt_gather_rows_indirect), all_to_all_single;
+  6. reorder received rows into local expert order, grouped GEMM (tcgen05);
+  7. gather result rows back in receive order, all_to_all_single back;
+  8. reorder into local assignment order (token-major, topk slots).
+"""
+
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from flashattentionanycard_b200 import _native
+
+
+# ----------------------------------------------------------------------------- planning
+@dataclass
+class Placement:
+    world: int
+    experts: int
+    replicas: np.ndarray  # int32 [E]
+    vbase: np.ndarray  # int32 [E]
+    v_expert: np.ndarray  # int32 [V]
+    v_replica: np.ndarray  # int32 [V]
+    v_rows: np.ndarray  # int64 [V] packed rows served
+    v_rank: np.ndarray  # int32 [V]
+    v_local: np.ndarray  # int32 [V] index among the rank's virtual experts
+    local: list = field(default_factory=list)  # per rank: ascending list of v
+    rank_rows: np.ndarray = None  # int64 [world] rows served per rank
+
+    @property
+    def virtual_experts(self):
+        return int(self.v_expert.size)
+
+
+def replica_rows(count, replicas):
+    """Rows of each replica when ``count`` packed rows are split so that row q
+    goes to replica q * replicas // count (bokt_ep_keys)."""
+    bounds = [-(-j * count // replicas) for j in range(replicas + 1)]  # ceil(j c / R)
+    return np.diff(np.asarray(bounds, dtype=np.int64))
+
+
+def plan_placement(counts, world, cap_fraction=0.25):
+    """Deterministic virtual-expert placement for ``world`` ranks.
+
+    Each expert gets R_e = ceil(c_e / cap) replicas with cap = cap_fraction *
+    total / world (R_e = 1 on one rank), then replicas are placed largest
+    first on the least-loaded rank (ties: lower rank).  The LPT bound keeps the
+    busiest rank within cap of the average."""
+    counts = np.asarray(counts, dtype=np.int64)
+    experts = counts.size
+    total = int(counts.sum())
+    if world < 1:
+        raise ValueError("world must be >= 1")
+    if world == 1:
+        replicas = np.ones(experts, dtype=np.int64)
+    else:
+        cap = max(1, -(-int(total * cap_fraction) // world))
+        replicas = np.maximum(1, -(-counts // cap))
+        replicas = np.minimum(replicas, world * 4)
+    vbase = np.concatenate([[0], np.cumsum(replicas)[:-1]]).astype(np.int64)
+    v_expert, v_replica, v_rows = [], [], []
+    for e in range(experts):
+        rows = replica_rows(int(counts[e]), int(replicas[e])) if counts[e] else np.zeros(
+            int(replicas[e]), np.int64)
+        for j in range(int(replicas[e])):
+            v_expert.append(e)
+            v_replica.append(j)
+            v_rows.append(int(rows[j]))
+    v_expert = np.asarray(v_expert, dtype=np.int32)
+    v_replica = np.asarray(v_replica, dtype=np.int32)
+    v_rows = np.asarray(v_rows, dtype=np.int64)
+    order = sorted(range(v_rows.size), key=lambda v: (-int(v_rows[v]), v))
+    load = np.zeros(world, dtype=np.int64)
+    v_rank = np.zeros(v_rows.size, dtype=np.int32)
+    for v in order:
+        r = int(np.argmin(load))  # first minimum: lowest rank on ties
+        v_rank[v] = r
+        load[r] += v_rows[v]
+    local = [sorted(int(v) for v in np.nonzero(v_rank == r)[0]) for r in range(world)]
+    v_local = np.zeros(v_rows.size, dtype=np.int32)
+    for r in range(world):
+        for i, v in enumerate(local[r]):
+            v_local[v] = i
+    return Placement(world, experts, replicas.astype(np.int32), vbase.astype(np.int32), v_expert,
+                     v_replica, v_rows, v_rank, v_local, local, load)
+
+
+@dataclass
+class Plan:
+    """Per-rank split sizes implied by a routing table and a placement."""
+
+    send: np.ndarray  # int64 [world, world]: rows rank r sends to rank d
+    local_rows: list  # per rank: int64 [n_local] rows per local virtual expert
+
+    def recv(self, rank):
+        return self.send[:, rank]
+
+
+def row_destinations(ids_flat, placement, topk, tokens_per_rank):
+    """(perm, owner[p], dest[p], v[p]) of every packed row of the global routing."""
+    ids_flat = np.asarray(ids_flat, dtype=np.int64)
+    e_count = np.bincount(ids_flat, minlength=placement.experts)
+    offsets = np.concatenate([[0], np.cumsum(e_count)])
+    perm = np.argsort(ids_flat, kind="stable")
+    e = ids_flat[perm]
+    q = np.arange(perm.size) - offsets[e]
+    reps = placement.replicas.astype(np.int64)[e]
+    j = np.where(e_count[e] > 0, (q * reps) // np.maximum(e_count[e], 1), 0)
+    v = placement.vbase.astype(np.int64)[e] + j
+    dest = placement.v_rank.astype(np.int64)[v]
+    owner = (perm // topk) // tokens_per_rank
+    return perm, owner, dest, v
+
+
+def plan_splits(ids_flat, placement, topk, tokens_per_rank):
+    world = placement.world
+    _, owner, dest, v = row_destinations(ids_flat, placement, topk, tokens_per_rank)
+    send = np.zeros((world, world), dtype=np.int64)
+    np.add.at(send, (owner, dest), 1)
+    local_rows = []
+    for r in range(world):
+        lv = placement.v_local.astype(np.int64)[v[dest == r]]
+        local_rows.append(np.bincount(lv, minlength=len(placement.local[r])).astype(np.int64))
+    return Plan(send, local_rows)
+
+
+# ----------------------------------------------------------------------------- device step
+class ExpertParallelMoE:
+    """One rank of the expert-parallel grouped GEMM.
+
+    ``local_weights``: [n_local, K, N] weights of this rank's virtual experts in
+    ``placement.local[rank]`` order (W[v_expert[v]]).  ``plan``: split sizes for
+    the routing the step will see; the step verifies them on the device."""
+
+    def __init__(self, local_weights, placement, plan, rank, world, topk, tokens_per_rank,
+                 group=None, params=None, sm_count=None):
+        import torch
+
+        from flashattentionanycard_b200.kernels.moe_routing import MoeRouter
+
+        self.rank, self.world, self.topk = rank, world, topk
+        self.tokens_per_rank = tokens_per_rank
+        self.group = group
+        self.params = dict(params or {})
+        self.w = local_weights
+        self.device = local_weights.device
+        dev = self.device
+        self.k, self.n = int(local_weights.shape[1]), int(local_weights.shape[2])
+        self.n_local = len(placement.local[rank])
+        if local_weights.shape[0] != self.n_local:
+            raise ValueError("local_weights must hold one [K, N] slice per local virtual expert")
+        self.sm = sm_count or torch.cuda.get_device_properties(dev).multi_processor_count
+        self.experts = placement.experts
+        self.a_global = tokens_per_rank * world * topk
+        self.a_local = tokens_per_rank * topk
+        i32 = dict(device=dev, dtype=torch.int32)
+        self.replicas = torch.tensor(placement.replicas, **i32)
+        self.vbase = torch.tensor(placement.vbase, **i32)
+        self.v_rank = torch.tensor(placement.v_rank, **i32)
+        self.v_local = torch.tensor(placement.v_local, **i32)
+        self.ids_global = torch.zeros(self.a_global, **i32)
+        self.route_global = MoeRouter(self.a_global, self.experts, dev)
+        self.route_send = MoeRouter(self.a_global, world + 1, dev)
+        self.route_recv = MoeRouter(self.a_global, world + 1, dev)
+        self.route_local = MoeRouter(self.a_global, self.n_local + 1, dev)
+        self.key_send = torch.zeros(self.a_global, **i32)
+        self.key_recv = torch.zeros(self.a_global, **i32)
+        self.key_local = torch.zeros(self.a_global, **i32)
+        self.send_sizes = [int(v) for v in plan.send[rank]]
+        self.recv_sizes = [int(v) for v in plan.recv(rank)]
+        self.n_send, self.n_recv = sum(self.send_sizes), sum(self.recv_sizes)
+        local_rows = plan.local_rows[rank]
+        self.expected_send = torch.tensor(self.send_sizes, **i32)
+        self.expected_recv = torch.tensor(self.recv_sizes, **i32)
+        self.expected_local = torch.tensor([int(v) for v in local_rows], **i32)
+        if int(local_rows.sum()) != self.n_recv:
+            raise ValueError("plan is inconsistent: local rows != received rows")
+        dt = local_weights.dtype
+        self.send_x = torch.empty(max(self.n_send, 1), self.k, device=dev, dtype=dt)
+        self.recv_x = torch.empty(max(self.n_recv, 1), self.k, device=dev, dtype=dt)
+        self.x_packed = torch.empty(max(self.n_recv, 1), self.k, device=dev, dtype=dt)
+        self.y_packed = torch.empty(max(self.n_recv, 1), self.n, device=dev, dtype=dt)
+        self.y_send = torch.empty(max(self.n_recv, 1), self.n, device=dev, dtype=dt)
+        self.y_ret = torch.empty(max(self.n_send, 1), self.n, device=dev, dtype=dt)
+        self.out = torch.empty(self.a_local, self.n, device=dev, dtype=dt)
+
+    # -- collectives (NCCL on GPU ranks) -------------------------------------------------
+    def _all_gather_ids(self, ids_local):
+        import torch.distributed as dist
+
+        if self.world == 1:
+            self.ids_global.copy_(ids_local.reshape(-1))
+        else:
+            dist.all_gather_into_tensor(self.ids_global, ids_local.reshape(-1), group=self.group)
+
+    def _all_to_all(self, out, inp, out_sizes, in_sizes):
+        import torch.distributed as dist
+
+        if self.world == 1:
+            if out_sizes[0]:
+                out[: out_sizes[0]].copy_(inp[: in_sizes[0]])
+            return
+        dist.all_to_all_single(out[: sum(out_sizes)], inp[: sum(in_sizes)],
+                               output_split_sizes=out_sizes, input_split_sizes=in_sizes,
+                               group=self.group)
+
+    # -- phases ----------------------------------------------------------------------------
+    def route(self):
+        """Global routing of self.ids_global, keys, the three orders, plan check."""
+        lib = _native.load()
+        stream = _native.current_stream(self.device)
+        g = self.route_global(self.ids_global)
+        _native.check(lib.bokt_ep_keys(
+            g.perm.data_ptr(), self.ids_global.data_ptr(), g.offsets.data_ptr(),
+            g.counts.data_ptr(), self.replicas.data_ptr(), self.vbase.data_ptr(),
+            self.v_rank.data_ptr(), self.v_local.data_ptr(), self.a_global, self.experts,
+            self.topk, self.tokens_per_rank, self.rank, self.world, self.n_local,
+            self.key_send.data_ptr(), self.key_recv.data_ptr(), self.key_local.data_ptr(),
+            stream), "bokt_ep_keys")
+        self.route_send(self.key_send)
+        self.route_recv(self.key_recv)
+        self.route_local(self.key_local)
+        for tag, (counts, expected) in enumerate(
+                ((self.route_send.counts, self.expected_send),
+                 (self.route_recv.counts, self.expected_recv),
+                 (self.route_local.counts, self.expected_local))):
+            n = expected.numel()
+            if n:
+                _native.check(lib.bokt_check_counts(counts.data_ptr(), expected.data_ptr(), n,
+                                                    tag + 1, stream), "bokt_check_counts")
+
+    def _gather(self, src, dst, rows, inner, outer, divisor=1, base=0):
+        if rows == 0:
+            return
+        lib = _native.load()
+        _native.check(lib.bokt_gather_rows_indirect(
+            src.data_ptr(), src.shape[0], dst.data_ptr(), inner.data_ptr(), inner.numel(),
+            outer.data_ptr() if outer is not None else None, rows, src.shape[1],
+            src.element_size(), divisor, base, _native.current_stream(self.device)),
+            "bokt_gather_rows_indirect")
+
+    def pack_send(self, x_local):
+        """send_x[i] = x of the token of the i-th row this rank sends (by destination)."""
+        g = self.route_global
+        self._gather(x_local, self.send_x, self.n_send, g.perm, self.route_send.perm,
+                     divisor=self.topk, base=self.rank * self.tokens_per_rank)
+
+    def unpack_recv(self):
+        """x_packed = received rows in local virtual-expert order."""
+        self._gather(self.recv_x, self.x_packed, self.n_recv, self.route_recv.inv_perm,
+                     self.route_local.perm)
+
+    def compute(self):
+        """Grouped GEMM over the local virtual experts (tcgen05)."""
+        from flashattentionanycard_b200.kernels import moe_grouped_gemm
+
+        if self.n_recv == 0:
+            return
+        offsets = self.route_local.offsets[: self.n_local + 1]
+        moe_grouped_gemm.launch(self.x_packed[: self.n_recv], self.w, offsets,
+                                self.y_packed[: self.n_recv], self.params, self.sm)
+
+    def pack_return(self):
+        """y_send = result rows in receive order (grouped by token owner)."""
+        self._gather(self.y_packed, self.y_send, self.n_recv, self.route_local.inv_perm,
+                     self.route_recv.perm)
+
+    def unpack_return(self):
+        """out = returned rows in local assignment order (token-major, topk slots)."""
+        g = self.route_global
+        outer = g.inv_perm[self.rank * self.a_local:(self.rank + 1) * self.a_local]
+        self._gather(self.y_ret, self.out, self.a_local, self.route_send.inv_perm, outer)
+        return self.out
+
+    def forward(self, x_local, ids_local):
+        """x_local [tokens_per_rank, K], ids_local [tokens_per_rank, topk] int32 ->
+        [tokens_per_rank * topk, N]: row t*topk + k = x[t] @ W[ids[t, k]]."""
+        self._all_gather_ids(ids_local)
+        self.route()
+        self.pack_send(x_local)
+        self._all_to_all(self.recv_x, self.send_x, self.recv_sizes, self.send_sizes)
+        self.unpack_recv()
+        self.compute()
+        self.pack_return()
+        self._all_to_all(self.y_ret, self.y_send, self.send_sizes, self.recv_sizes)
+        return self.unpack_return()
+
+
+def local_weight_slices(placement, rank):
+    """Global expert index of each local virtual expert of ``rank``."""
+    return [int(placement.v_expert[v]) for v in placement.local[rank]]

@@ -176,6 +176,45 @@ int bokt_moe_route_noalloc(const int32_t* expert_ids, int A, int E, int32_t* cou
 int bokt_gather_rows(const void* src, int64_t src_rows, void* dst, const int32_t* index, int rows,
                      int cols, int elem_bytes, int divisor, void* stream);
 
+/*
+ * Two-level row gather for expert-parallel dispatch / combine:
+ *   dst[j, :] = src[inner[outer[j]] / divisor - base, :]   (outer == NULL: inner[j])
+ * inner has inner_len entries, src has src_rows rows of cols elements.  A
+ * source outside src sets the device status word; the row is left unwritten.
+ * No counterpart in the reference (single GPU only).
+ */
+int bokt_gather_rows_indirect(const void* src, int64_t src_rows, void* dst, const int32_t* inner,
+                              int64_t inner_len, const int32_t* outer, int rows, int cols,
+                              int elem_bytes, int divisor, int64_t base, void* stream);
+
+/*
+ * Expert-parallel sort keys of every packed row p of the global routing, as
+ * seen by rank `me` of `world` (tokens owned in contiguous blocks of
+ * tokens_per_rank).  Expert e is served by replicas[e] virtual experts
+ * vbase[e] .. vbase[e] + replicas[e] - 1 that split its packed rows
+ * contiguously (row q of the expert goes to replica q * replicas[e] / counts[e]);
+ * v_rank[v] is the rank serving virtual expert v and v_local[v] its index
+ * among that rank's virtual experts.  Outputs (int32[A]):
+ *   key_send[p]  = destination rank if this rank owns the token, else world
+ *   key_recv[p]  = owning rank if this rank serves the row, else world
+ *   key_local[p] = local virtual-expert index if this rank serves it, else n_local
+ * Sorting each key with bokt_moe_route gives the send order, the receive order
+ * and the local grouped-GEMM order.  No counterpart in the reference.
+ */
+int bokt_ep_keys(const int32_t* perm, const int32_t* ids, const int32_t* offsets,
+                 const int32_t* counts, const int32_t* replicas, const int32_t* vbase,
+                 const int32_t* v_rank, const int32_t* v_local, int A, int E, int topk,
+                 int tokens_per_rank, int me, int world, int n_local, int32_t* key_send,
+                 int32_t* key_recv, int32_t* key_local, void* stream);
+
+/*
+ * Sets the device status word (code 3, detail tag * 65536 + i) where
+ * counts[i] != expected[i]: the split sizes an expert-parallel plan fixed for
+ * NCCL no longer match the routing.  No counterpart in the reference.
+ */
+int bokt_check_counts(const int32_t* counts, const int32_t* expected, int n, int tag,
+                      void* stream);
+
 /* Resource usage of the kernel a call with these arguments would launch. */
 int bokt_kernel_attrs(int kernel, int dtype, int n, int k, const bokt_params* params,
                       bokt_attrs* out);

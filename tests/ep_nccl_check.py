@@ -1,0 +1,60 @@
+"""torchrun worker for tests/test_gpu_expert_parallel.py::test_nccl_two_ranks.
+
+Each rank owns a block of tokens, holds only its virtual experts' weights, and
+runs ExpertParallelMoE.forward with NCCL all-gather / all-to-all.  Rank outputs
+are checked against x[token] @ W[expert] (fp32) with the reference gate.
+"""
+
+import os
+import sys
+from datetime import timedelta
+from pathlib import Path
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+
+from flashattentionanycard_b200 import _native  # noqa: E402
+from flashattentionanycard_b200 import expert_parallel as ep  # noqa: E402
+from flashattentionanycard_b200.workloads import zipf_routing  # noqa: E402
+from oracle import numerics  # noqa: E402
+
+
+def main():
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", rank)))
+    torch.cuda.set_device(device)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=60), device_id=device)
+    tokens, experts, k, n = 4096, 16, 256, 512
+    tpr = tokens // world
+    ids_all = zipf_routing(tokens, experts, 2, 1.1, 8).reshape(-1)
+    g = torch.Generator().manual_seed(8)
+    x = torch.randn(tokens, k, generator=g).bfloat16()
+    w = (0.05 * torch.randn(experts, k, n, generator=g)).bfloat16()
+    ids = ids_all.numpy()
+    placement = ep.plan_placement(np.bincount(ids, minlength=experts), world)
+    plan = ep.plan_splits(ids, placement, 2, tpr)
+    lw = w[ep.local_weight_slices(placement, rank)].contiguous().to(device)
+    m = ep.ExpertParallelMoE(lw, placement, plan, rank, world, 2, tpr)
+    ids_local = ids_all[rank * tpr * 2:(rank + 1) * tpr * 2].to(torch.int32).to(device)
+    out = None
+    for _ in range(2):  # twice: buffers are reused across steps
+        out = m.forward(x[rank * tpr:(rank + 1) * tpr].to(device), ids_local)
+    torch.cuda.synchronize()
+    code, detail = _native.device_status(reset=True)
+    a = np.arange(rank * tpr * 2, (rank + 1) * tpr * 2)
+    ref = np.einsum("ak,akn->an", x.float().numpy()[a // 2], w.float().numpy()[ids[a]])
+    stats = numerics.check_output(out.float().cpu().numpy(), ref, "bf16")
+    ok = torch.tensor([1 if code == 0 else 0], device=device)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    dist.barrier()
+    dist.destroy_process_group()
+    if rank == 0 and ok.item() == 1:
+        print(f"EP_NCCL_OK rel={stats['normwise_rel_error']:.2e}")
+    return 0 if code == 0 else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())
