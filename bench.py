@@ -41,6 +41,7 @@ sys.path.insert(0, str(REPO))
 METRIC = "TFLOP/s (GEMM, MoE grouped GEMM) & RMSNorm GB/s vs B200 peak at 1–8 GPUs"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 L2_BYTES = 126 * 1024 * 1024
+EP_COMM = "peer"  # --ep-comm: expert-parallel dispatch/combine over NVLink peer stores or NCCL
 # Rotating input sets together span 4x L2, so a set is long evicted when it is reused.
 ROTATION_BYTES = 4 * L2_BYTES
 
@@ -463,14 +464,23 @@ class MoeLarge:
         del self.x
         self.ids_local = ids.reshape(-1)[rank * tpr * cfg["topk"]:(rank + 1) * tpr * cfg["topk"]]
         self.ids_local = self.ids_local.to(torch_int32()).to(device)
-        self.ep = ep.ExpertParallelMoE(local, self.placement, self.plan, rank, world,
-                                       cfg["topk"], tpr, group=dist.group.WORLD,
-                                       params=self.params, sm_count=self.sm)
+        self.comm = EP_COMM
+        if self.comm == "peer":
+            self.ep = ep.PeerExpertParallelMoE(local, self.placement, self.plan, rank, world,
+                                               cfg["topk"], tpr, group=dist.group.WORLD,
+                                               params=self.params, sm_count=self.sm)
+            self.launches_per_step = 7  # route x3, plan, rowmap, dispatch, grouped GEMM
+        else:
+            self.ep = ep.ExpertParallelMoE(local, self.placement, self.plan, rank, world,
+                                           cfg["topk"], tpr, group=dist.group.WORLD,
+                                           params=self.params, sm_count=self.sm)
+            self.launches_per_step = 21  # routing/keys/sorts/checks + 4 gathers + GEMM
         import torch
 
         torch.cuda.empty_cache()
-        self.launches_per_step = 21  # 16 routing/keys/sorts/checks + 4 gathers + grouped GEMM
-        self.graphable = False  # NCCL all-to-all with plan split sizes: timed eagerly
+        self.graphable = False  # collectives between kernels: timed eagerly
+        rows = int(self.placement.rank_rows[rank])
+        self.kernel_flops = 2.0 * rows * cfg["k"] * cfg["n"]
 
     def step(self, i):
         from flashattentionanycard_b200.kernels import moe_grouped_gemm
@@ -492,11 +502,15 @@ class MoeLarge:
                "params": self.params}
         if world > 1:
             p = self.placement
+            step = ("all-gather ids + route + NVLink peer-store dispatch + grouped GEMM with "
+                    "peer-store combine epilogue, one-word all-reduce barriers, eager"
+                    if self.comm == "peer" else
+                    "all-gather ids + route + dispatch all-to-all + grouped GEMM + "
+                    "combine all-to-all (NCCL), eager")
             out.update({
                 "partition": f"expert-parallel over {world} GPUs: {p.virtual_experts} virtual "
                              f"experts (hot experts replicated, rows split), LPT placement",
-                "step": "all-gather ids + route + dispatch all-to-all + grouped GEMM + "
-                        "combine all-to-all (NCCL), eager",
+                "step": step, "ep_comm": self.comm,
                 "rows_per_rank": [int(v) for v in p.rank_rows],
                 "max_replicas": int(p.replicas.max()),
             })
@@ -800,7 +814,8 @@ def run_ours(args):
         peak = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
         unit_r = "GB/s"
     else:
-        achieved = workload.flops_per_step / (kernel_ms / 1e3) / 1e12
+        flops = getattr(workload, "kernel_flops", workload.flops_per_step)
+        achieved = flops / (kernel_ms / 1e3) / 1e12
         peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
         unit_r = "TFLOP/s"
     traffic, traffic_source = profile_traffic(workload.name)
@@ -872,7 +887,10 @@ def _last_kernel(workload, i):  # noqa: ARG001 - same inputs every launch
     from flashattentionanycard_b200.kernels import moe_grouped_gemm
 
     if getattr(workload, "world", 1) > 1:
-        workload.ep.compute()
+        if workload.comm == "peer":
+            workload.ep.compute_and_combine()
+        else:
+            workload.ep.compute()
         return
 
     moe_grouped_gemm.launch(workload.packed, workload.w, workload.router.offsets, workload.y,
@@ -888,7 +906,11 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="rmsnorm")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ep-comm", choices=("peer", "nccl"), default="peer",
+                    help="moe_large at N>1: NVLink peer stores (fused) or NCCL all-to-all")
     args = ap.parse_args()
+    global EP_COMM
+    EP_COMM = args.ep_comm
     if args.steps is None:
         args.steps = 20 if args.impl == "reference" else DEFAULT_STEPS[args.workload]
     if args.warmup < 3:

@@ -172,27 +172,30 @@ int encode_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dim
 // ----------------------------------------------------------------- GEMM dispatch
 using bokt::GemmTcArgs;
 
-template <int BN, bool GROUPED, typename T>
+template <int BN, bool GROUPED, typename T, bool SCATTER>
 const void* tc_kernel_ptr() {
-  return reinterpret_cast<const void*>(&bokt::gemm_tc_kernel<BN, GROUPED, T>);
+  return reinterpret_cast<const void*>(&bokt::gemm_tc_kernel<BN, GROUPED, T, SCATTER>);
 }
 
-template <bool GROUPED, typename T>
+template <bool GROUPED, typename T, bool SCATTER>
 const void* tc_kernel_for(int bn) {
   switch (bn) {
-    case 64: return tc_kernel_ptr<64, GROUPED, T>();
-    case 128: return tc_kernel_ptr<128, GROUPED, T>();
-    case 256: return tc_kernel_ptr<256, GROUPED, T>();
+    case 64: return tc_kernel_ptr<64, GROUPED, T, SCATTER>();
+    case 128: return tc_kernel_ptr<128, GROUPED, T, SCATTER>();
+    case 256: return tc_kernel_ptr<256, GROUPED, T, SCATTER>();
   }
   return nullptr;
 }
 
-const void* tc_kernel(bool grouped, int dtype, int bn) {
+const void* tc_kernel(bool grouped, int dtype, int bn, bool scatter = false) {
+  if (scatter)
+    return dtype == BOKT_BF16 ? tc_kernel_for<true, __nv_bfloat16, true>(bn)
+                              : tc_kernel_for<true, __half, true>(bn);
   if (grouped)
-    return dtype == BOKT_BF16 ? tc_kernel_for<true, __nv_bfloat16>(bn)
-                              : tc_kernel_for<true, __half>(bn);
-  return dtype == BOKT_BF16 ? tc_kernel_for<false, __nv_bfloat16>(bn)
-                            : tc_kernel_for<false, __half>(bn);
+    return dtype == BOKT_BF16 ? tc_kernel_for<true, __nv_bfloat16, false>(bn)
+                              : tc_kernel_for<true, __half, false>(bn);
+  return dtype == BOKT_BF16 ? tc_kernel_for<false, __nv_bfloat16, false>(bn)
+                            : tc_kernel_for<false, __half, false>(bn);
 }
 
 struct TcConfig {
@@ -232,8 +235,9 @@ int resolve_tc_config(const bokt_params* p, bool grouped, int experts, int smem_
 }
 
 int launch_tc(bool grouped, int dtype, const TcConfig& cfg, const CUtensorMap& ma,
-              const CUtensorMap& mb, const GemmTcArgs& args, int grid, cudaStream_t s) {
-  const void* fn = tc_kernel(grouped, dtype, cfg.bn);
+              const CUtensorMap& mb, const GemmTcArgs& args, int grid, cudaStream_t s,
+              bool scatter = false) {
+  const void* fn = tc_kernel(grouped, dtype, cfg.bn, scatter);
   int rc = ensure_smem(fn, cfg.smem);
   if (rc) return rc;
   void* kargs[] = {const_cast<CUtensorMap*>(&ma), const_cast<CUtensorMap*>(&mb),
@@ -374,10 +378,22 @@ int bokt_gemm(const void* A, const void* B, void* C, int M, int N, int K, int dt
   return launch_tc(false, dtype, cfg, ma, mb, args, grid, s);
 }
 
-int bokt_moe_grouped_gemm(const void* X, const void* W, const void* offsets, int offsets_is_i64,
-                          void* Y, int T, int E, int N, int K, int dtype, int sm_count,
-                          const bokt_params* params, void* stream) {
-  g_err[0] = 0;
+}  // extern "C"
+
+namespace {
+
+// Shared body of the grouped GEMM entry points; scatter != nullptr selects the
+// expert-parallel epilogue that sends each packed row to its owner's buffer.
+struct ScatterArgs {
+  const int32_t* rowmap;
+  void* const* out_ptrs;
+  int rows_per_owner;
+  int owners;
+};
+
+int grouped_gemm_impl(const void* X, const void* W, const void* offsets, int offsets_is_i64,
+                      void* Y, int T, int E, int N, int K, int dtype, int sm_count,
+                      const bokt_params* params, void* stream, const ScatterArgs* scatter) {
   if (dtype != BOKT_FP16 && dtype != BOKT_BF16) return fail(BOKT_ERR_INVALID, "dtype %d", dtype);
   if (T < 0 || E < 0 || N < 0 || K < 0) return fail(BOKT_ERR_INVALID, "negative size");
   if (E > bokt::kGemmMaxExperts)
@@ -389,6 +405,9 @@ int bokt_moe_grouped_gemm(const void* X, const void* W, const void* offsets, int
   int rc = device_info(&dev);
   if (rc) return rc;
   if (!tc_eligible(X, W, Y, N, K)) {
+    if (scatter)
+      return fail(BOKT_ERR_UNSUPPORTED,
+                  "scatter epilogue needs the tcgen05 path (K, N multiples of 8, aligned)");
     return dtype == BOKT_BF16
                ? launch_simt<__nv_bfloat16>(X, W, Y, T, N, K, offsets, offsets_is_i64, E, s)
                : launch_simt<__half>(X, W, Y, T, N, K, offsets, offsets_is_i64, E, s);
@@ -418,6 +437,12 @@ int bokt_moe_grouped_gemm(const void* X, const void* W, const void* offsets, int
   args.offsets = offsets;
   args.offsets_i64 = offsets_is_i64 ? 1 : 0;
   args.E = E;
+  if (scatter) {
+    args.rowmap = scatter->rowmap;
+    args.out_ptrs = scatter->out_ptrs;
+    args.rows_per_owner = scatter->rows_per_owner;
+    args.owners = scatter->owners;
+  }
   const bokt_params zero = {};
   const int mult = param_or((params ? params : &zero)->cta_multiplier, 1);
   const int sms = sm_count > 0 ? sm_count : dev.sm_count;
@@ -426,7 +451,96 @@ int bokt_moe_grouped_gemm(const void* X, const void* W, const void* offsets, int
   long long grid = (long long)sms * mult;
   if (grid > max_tiles) grid = max_tiles;
   if (grid < 1) grid = 1;
-  return launch_tc(true, dtype, cfg, ma, mb, args, int(grid), s);
+  return launch_tc(true, dtype, cfg, ma, mb, args, int(grid), s, scatter != nullptr);
+}
+
+}  // namespace
+
+extern "C" {
+
+int bokt_moe_grouped_gemm(const void* X, const void* W, const void* offsets, int offsets_is_i64,
+                          void* Y, int T, int E, int N, int K, int dtype, int sm_count,
+                          const bokt_params* params, void* stream) {
+  g_err[0] = 0;
+  return grouped_gemm_impl(X, W, offsets, offsets_is_i64, Y, T, E, N, K, dtype, sm_count, params,
+                           stream, nullptr);
+}
+
+int bokt_moe_grouped_gemm_scatter(const void* X, const void* W, const void* offsets,
+                                  int offsets_is_i64, int T, int E, int N, int K, int dtype,
+                                  int sm_count, const int32_t* rowmap, void* const* out_ptrs,
+                                  int rows_per_owner, int owners, const bokt_params* params,
+                                  void* stream) {
+  g_err[0] = 0;
+  if (!rowmap || !out_ptrs || rows_per_owner <= 0 || owners <= 0)
+    return fail(BOKT_ERR_INVALID, "scatter needs rowmap, out_ptrs, rows_per_owner, owners");
+  const ScatterArgs sc = {rowmap, out_ptrs, rows_per_owner, owners};
+  // Y is unused by the scatter epilogue; any valid aligned pointer satisfies the path checks.
+  return grouped_gemm_impl(X, W, offsets, offsets_is_i64, const_cast<void*>(X), T, E, N, K,
+                           dtype, sm_count, params, stream, &sc);
+}
+
+int bokt_ep_plan(const int32_t* counts, const int32_t* offsets, const int32_t* replicas, int E,
+                 const int32_t* v_rank, int V, int world, int me, const int32_t* capacity,
+                 int32_t* v_plo, int32_t* v_size, int32_t* v_lbase, int32_t* loffs,
+                 int32_t* rank_rows, void* stream) {
+  g_err[0] = 0;
+  if (E <= 0 || V <= 0 || world <= 0 || me < 0 || me >= world)
+    return fail(BOKT_ERR_INVALID, "bad size");
+  if (!counts || !offsets || !replicas || !v_rank || !capacity || !v_plo || !v_size ||
+      !v_lbase || !loffs || !rank_rows)
+    return fail(BOKT_ERR_INVALID, "null pointer");
+  cudaError_t e = launch(bokt::ep_plan_kernel, dim3(1), dim3(32), 0,
+                         static_cast<cudaStream_t>(stream), counts, offsets, replicas, E, v_rank,
+                         V, world, me, capacity, v_plo, v_size, v_lbase, loffs, rank_rows);
+  if (e != cudaSuccess) return cuda_fail(e, "ep_plan launch");
+  return BOKT_OK;
+}
+
+int bokt_ep_dispatch(const void* x_local, int cols, int elem_bytes, const int32_t* ids,
+                     const int32_t* inv_perm, const int32_t* offsets, const int32_t* counts,
+                     const int32_t* replicas, const int32_t* vbase, const int32_t* v_rank,
+                     const int32_t* v_plo, const int32_t* v_lbase, void* const* xpk_ptrs,
+                     const int32_t* capacity, int a_local, int topk, int me, int E,
+                     void* stream) {
+  g_err[0] = 0;
+  if (cols <= 0 || elem_bytes <= 0 || a_local < 0 || topk <= 0 || me < 0 || E <= 0)
+    return fail(BOKT_ERR_INVALID, "bad size");
+  if (a_local == 0) return BOKT_OK;
+  const long long row_bytes = (long long)cols * elem_bytes;
+  if (row_bytes % 16 != 0 || !aligned16(x_local))
+    return fail(BOKT_ERR_UNSUPPORTED, "dispatch rows must be 16-byte multiples, 16-byte aligned");
+  if (!ids || !inv_perm || !offsets || !counts || !replicas || !vbase || !v_rank || !v_plo ||
+      !v_lbase || !xpk_ptrs || !capacity)
+    return fail(BOKT_ERR_INVALID, "null pointer");
+  const int warps_per_block = 8;
+  int grid = (a_local + warps_per_block - 1) / warps_per_block;
+  if (grid > 148 * 16) grid = 148 * 16;
+  cudaError_t e = launch(bokt::ep_dispatch_kernel, dim3(grid), dim3(32 * warps_per_block), 0,
+                         static_cast<cudaStream_t>(stream), static_cast<const uint4*>(x_local),
+                         int(row_bytes / 16), ids, inv_perm, offsets, counts, replicas, vbase,
+                         v_rank, v_plo, v_lbase, reinterpret_cast<uint4* const*>(xpk_ptrs),
+                         capacity, a_local, topk, me, E);
+  if (e != cudaSuccess) return cuda_fail(e, "ep_dispatch launch");
+  return BOKT_OK;
+}
+
+int bokt_ep_rowmap(const int32_t* perm, const int32_t* ids, const int32_t* offsets,
+                   const int32_t* counts, const int32_t* replicas, const int32_t* vbase,
+                   const int32_t* v_rank, const int32_t* v_plo, const int32_t* v_lbase, int A,
+                   int E, int me, int capacity, int32_t* rowmap, void* stream) {
+  g_err[0] = 0;
+  if (A < 0 || E <= 0 || me < 0 || capacity < 0) return fail(BOKT_ERR_INVALID, "bad size");
+  if (A == 0) return BOKT_OK;
+  if (!perm || !ids || !offsets || !counts || !replicas || !vbase || !v_rank || !v_plo ||
+      !v_lbase || !rowmap)
+    return fail(BOKT_ERR_INVALID, "null pointer");
+  const int grid = (A + 255) / 256 < 4096 ? (A + 255) / 256 : 4096;
+  cudaError_t e = launch(bokt::ep_rowmap_kernel, dim3(grid), dim3(256), 0,
+                         static_cast<cudaStream_t>(stream), perm, ids, offsets, counts, replicas,
+                         vbase, v_rank, v_plo, v_lbase, A, E, me, capacity, rowmap);
+  if (e != cudaSuccess) return cuda_fail(e, "ep_rowmap launch");
+  return BOKT_OK;
 }
 
 int bokt_rmsnorm(const void* X, const void* W, void* Y, int M, int N, float eps, int dtype,
@@ -558,6 +672,53 @@ int bokt_check_counts(const int32_t* counts, const int32_t* expected, int n, int
   cudaError_t e = launch(bokt::check_counts_kernel, dim3(1), dim3(256), 0,
                          static_cast<cudaStream_t>(stream), counts, expected, n, tag);
   if (e != cudaSuccess) return cuda_fail(e, "check_counts launch");
+  return BOKT_OK;
+}
+
+int bokt_ipc_export(const void* ptr, void* handle_out, int64_t* offset_out) {
+  g_err[0] = 0;
+  if (!ptr || !handle_out || !offset_out) return fail(BOKT_ERR_INVALID, "null pointer");
+  static PFN_cuMemGetAddressRange_v3020 get_range = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_range = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(fn);
+  });
+  if (!get_range) return fail(BOKT_ERR_CUDA, "cuMemGetAddressRange entry point unavailable");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  CUresult r = get_range(&base, &size, reinterpret_cast<CUdeviceptr>(ptr));
+  if (r != CUDA_SUCCESS) return fail(BOKT_ERR_CUDA, "cuMemGetAddressRange failed (%d)", int(r));
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  memcpy(handle_out, &h, sizeof(h));
+  *offset_out = int64_t(reinterpret_cast<uintptr_t>(ptr) - uintptr_t(base));
+  return BOKT_OK;
+}
+
+int bokt_ipc_import(const void* handle, int64_t offset, void** base_out, void** ptr_out) {
+  g_err[0] = 0;
+  if (!handle || !base_out || !ptr_out || offset < 0) return fail(BOKT_ERR_INVALID, "bad argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  *base_out = base;
+  *ptr_out = static_cast<char*>(base) + offset;
+  return BOKT_OK;
+}
+
+int bokt_ipc_close(void* base) {
+  g_err[0] = 0;
+  if (!base) return BOKT_OK;
+  cudaError_t e = cudaIpcCloseMemHandle(base);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcCloseMemHandle");
   return BOKT_OK;
 }
 

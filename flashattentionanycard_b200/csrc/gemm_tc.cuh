@@ -38,6 +38,13 @@ struct GemmTcArgs {
   const void* offsets;  // grouped only: E+1 offsets
   int offsets_i64;
   int E;
+  // Scatter epilogue (expert-parallel combine): packed row l goes to row
+  // rowmap[l] - o * rows_per_owner of out_ptrs[o], o = rowmap[l] / rows_per_owner;
+  // out_ptrs[o] may be a peer GPU's buffer (NVLink stores).
+  const int32_t* rowmap;
+  void* const* out_ptrs;
+  int rows_per_owner;
+  int owners;
 };
 
 template <int BN>
@@ -110,7 +117,7 @@ __device__ __forceinline__ TileCoord grouped_tile(int t, const int* tile_prefix,
   return c;
 }
 
-template <int BN, bool GROUPED, typename OutT>
+template <int BN, bool GROUPED, typename OutT, bool SCATTER = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    GemmTcArgs args) {
@@ -293,8 +300,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      const bool row_ok = r < tc.rows_valid;
+      bool row_ok = r < tc.rows_valid;
       OutT* crow = C + static_cast<size_t>(tc.c_row + (row_ok ? r : 0)) * N + tc.n0;
+      if constexpr (SCATTER) {
+        if (row_ok) {
+          const int a = args.rowmap[tc.c_row + r];
+          const int o = a / args.rows_per_owner;
+          if (a < 0 || o >= args.owners) {
+            report_status(kStatusBadExpertId, tc.c_row + r);
+            row_ok = false;
+          } else {
+            crow = reinterpret_cast<OutT*>(args.out_ptrs[o]) +
+                   static_cast<size_t>(a - o * args.rows_per_owner) * N + tc.n0;
+          }
+        }
+      }
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         uint32_t v[32];
@@ -317,6 +337,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
     }
+    if constexpr (SCATTER) __threadfence_system();  // peer stores visible before the barrier
   }
 
   // ---------------------------------------------------------------- teardown

@@ -270,3 +270,131 @@ __global__ void check_counts_kernel(const int32_t* __restrict__ counts,
 }
 
 }  // namespace bokt
+
+namespace bokt {
+
+constexpr int kStatusCapacity = 4;
+
+// Per-step expert-parallel layout from the global routing (one CTA, serial
+// over virtual experts; V is at most a few hundred).  Virtual expert v =
+// (expert e, replica j) serves the contiguous packed rows
+// [v_plo[v], v_plo[v] + v_size[v]) of the global routing; on its rank it is
+// stored at rows [v_lbase[v], v_lbase[v] + v_size[v]) of the packed buffer,
+// virtual experts in ascending v.  loffs = the local grouped-GEMM offsets of
+// rank `me` (n_local + 1 entries).  rank_rows[r] = rows rank r serves; a rank
+// over its buffer capacity is reported (kStatusCapacity).
+__global__ void ep_plan_kernel(const int32_t* __restrict__ counts,
+                               const int32_t* __restrict__ offsets,
+                               const int32_t* __restrict__ replicas, int E,
+                               const int32_t* __restrict__ v_rank, int V, int world, int me,
+                               const int32_t* __restrict__ capacity,
+                               int32_t* __restrict__ v_plo, int32_t* __restrict__ v_size,
+                               int32_t* __restrict__ v_lbase, int32_t* __restrict__ loffs,
+                               int32_t* __restrict__ rank_rows) {
+  pdl_allow_next();
+  pdl_wait();
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  int v = 0;
+  for (int e = 0; e < E; ++e) {
+    const long long c = counts[e];
+    const int R = replicas[e];
+    for (int j = 0; j < R; ++j, ++v) {
+      const long long lo = (static_cast<long long>(j) * c + R - 1) / R;  // ceil(j c / R)
+      const long long hi = (static_cast<long long>(j + 1) * c + R - 1) / R;
+      v_plo[v] = offsets[e] + static_cast<int>(lo);
+      v_size[v] = static_cast<int>(hi - lo);
+    }
+  }
+  for (int r = 0; r < world; ++r) rank_rows[r] = 0;
+  int nl = 0;
+  loffs[0] = 0;
+  for (v = 0; v < V; ++v) {
+    const int r = v_rank[v];
+    v_lbase[v] = rank_rows[r];
+    rank_rows[r] += v_size[v];
+    if (r == me) loffs[++nl] = rank_rows[r];
+  }
+  for (int r = 0; r < world; ++r)
+    if (rank_rows[r] > capacity[r]) report_status(kStatusCapacity, r);
+}
+
+__device__ __forceinline__ int ep_virtual_expert(int p, int e, const int32_t* offsets,
+                                                 const int32_t* counts, const int32_t* replicas,
+                                                 const int32_t* vbase) {
+  const long long q = p - offsets[e];
+  const int c = counts[e];
+  const int j = c > 0 ? static_cast<int>((q * replicas[e]) / c) : 0;
+  return vbase[e] + j;
+}
+
+// Dispatch over NVLink: every local assignment a_loc of this rank copies its
+// token's row into the packed buffer of the rank serving it (xpk[d] may be a
+// peer GPU's memory), at that rank's local position.  One warp per row,
+// 16-byte vectors.  Positions beyond the destination's capacity are reported
+// and skipped.
+__global__ void ep_dispatch_kernel(const uint4* __restrict__ x_local, int row_vecs,
+                                   const int32_t* __restrict__ ids,
+                                   const int32_t* __restrict__ inv_perm,
+                                   const int32_t* __restrict__ offsets,
+                                   const int32_t* __restrict__ counts,
+                                   const int32_t* __restrict__ replicas,
+                                   const int32_t* __restrict__ vbase,
+                                   const int32_t* __restrict__ v_rank,
+                                   const int32_t* __restrict__ v_plo,
+                                   const int32_t* __restrict__ v_lbase,
+                                   uint4* const* __restrict__ xpk,
+                                   const int32_t* __restrict__ capacity, int a_local,
+                                   int topk, int me, int E) {
+  pdl_allow_next();
+  pdl_wait();
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  for (int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < a_local; i += warps) {
+    const int a = me * a_local + i;
+    const int e = ids[a];
+    if (e < 0 || e >= E) {
+      if (lane == 0) report_status(kStatusBadExpertId, a);
+      continue;
+    }
+    const int p = inv_perm[a];
+    const int v = ep_virtual_expert(p, e, offsets, counts, replicas, vbase);
+    const int d = v_rank[v];
+    const int pos = v_lbase[v] + (p - v_plo[v]);
+    if (pos < 0 || pos >= capacity[d]) {
+      if (lane == 0) report_status(kStatusCapacity, a);
+      continue;
+    }
+    const uint4* src = x_local + static_cast<long long>(i / topk) * row_vecs;
+    uint4* dst = xpk[d] + static_cast<long long>(pos) * row_vecs;
+    for (int c = lane; c < row_vecs; c += 32) dst[c] = src[c];
+  }
+  __threadfence_system();  // peer stores visible system-wide before the next barrier
+}
+
+// For every packed row this rank serves: rowmap[local row] = global assignment
+// index (the grouped GEMM's scatter epilogue sends the row to that
+// assignment's owner).
+__global__ void ep_rowmap_kernel(const int32_t* __restrict__ perm,
+                                 const int32_t* __restrict__ ids,
+                                 const int32_t* __restrict__ offsets,
+                                 const int32_t* __restrict__ counts,
+                                 const int32_t* __restrict__ replicas,
+                                 const int32_t* __restrict__ vbase,
+                                 const int32_t* __restrict__ v_rank,
+                                 const int32_t* __restrict__ v_plo,
+                                 const int32_t* __restrict__ v_lbase, int A, int E, int me,
+                                 int capacity, int32_t* __restrict__ rowmap) {
+  pdl_allow_next();
+  pdl_wait();
+  for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < A; p += gridDim.x * blockDim.x) {
+    const int a = perm[p];
+    const int e = (a >= 0 && a < A) ? ids[a] : -1;
+    if (e < 0 || e >= E) continue;  // reported by the routing kernels
+    const int v = ep_virtual_expert(p, e, offsets, counts, replicas, vbase);
+    if (v_rank[v] != me) continue;
+    const int l = v_lbase[v] + (p - v_plo[v]);
+    if (l >= 0 && l < capacity) rowmap[l] = a;
+  }
+}
+
+}  // namespace bokt

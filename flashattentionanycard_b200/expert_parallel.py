@@ -29,6 +29,7 @@ One step (every rank, same order of collectives):
   8. reorder into local assignment order (token-major, topk slots).
 """
 
+import ctypes
 from dataclasses import dataclass, field
 
 import numpy as np
@@ -313,3 +314,199 @@ class ExpertParallelMoE:
 def local_weight_slices(placement, rank):
     """Global expert index of each local virtual expert of ``rank``."""
     return [int(placement.v_expert[v]) for v in placement.local[rank]]
+
+
+# ----------------------------------------------------------------------------- peer-memory step
+def _ptr_array(ptrs, device):
+    import torch
+
+    return torch.tensor([int(p) for p in ptrs], dtype=torch.int64, device=device)
+
+
+class PeerExpertParallelMoE:
+    """One rank of the expert-parallel grouped GEMM with dispatch and combine
+    over NVLink peer memory instead of NCCL all-to-all.
+
+    Each rank exports (CUDA IPC) its packed-input buffer and its output buffer
+    and maps the other ranks'.  A step:
+
+      1. all-gather the expert ids (NCCL; also orders this step after every
+         rank's previous step);
+      2. global routing (bokt_moe_route) and the per-step layout (bokt_ep_plan):
+         where each virtual expert's rows live on its rank;
+      3. bokt_ep_rowmap: the owner row of every row this rank will compute;
+      4. bokt_ep_dispatch: each token row is stored straight into the serving
+         rank's packed buffer (NVLink stores), then a one-word all-reduce
+         barrier;
+      5. bokt_moe_grouped_gemm_scatter: the tcgen05 grouped GEMM whose epilogue
+         stores every result row into its token owner's output buffer (NVLink
+         stores, overlapped with the remaining tiles), then the barrier.
+
+    No row gathers and no all-to-all: every row crosses NVLink once each way,
+    written by the kernel that produced it."""
+
+    def __init__(self, local_weights, placement, plan, rank, world, topk, tokens_per_rank,
+                 group=None, params=None, sm_count=None, exchange=True):
+        """``exchange=False`` skips the IPC pointer exchange: the caller sets the
+        per-rank pointers with ``set_peer_pointers`` (ranks sharing one process)."""
+        import torch
+
+        from flashattentionanycard_b200.kernels.moe_routing import MoeRouter
+
+        lib = _native.load()
+        self.rank, self.world, self.topk = rank, world, topk
+        self.tokens_per_rank = tokens_per_rank
+        self.group = group
+        self.params = _native.make_params(params or {})
+        self.w = local_weights
+        self.device = dev = local_weights.device
+        self.k, self.n = int(local_weights.shape[1]), int(local_weights.shape[2])
+        self.n_local = len(placement.local[rank])
+        if local_weights.shape[0] != self.n_local:
+            raise ValueError("local_weights must hold one [K, N] slice per local virtual expert")
+        if self.n_local == 0:
+            raise ValueError("every rank must serve at least one virtual expert")
+        self.sm = sm_count or torch.cuda.get_device_properties(dev).multi_processor_count
+        self.dtype = _native.dtype_code(local_weights.dtype)
+        self.experts = placement.experts
+        self.V = placement.virtual_experts
+        self.a_global = tokens_per_rank * world * topk
+        self.a_local = tokens_per_rank * topk
+        i32 = dict(device=dev, dtype=torch.int32)
+        self.replicas = torch.tensor(placement.replicas, **i32)
+        self.vbase = torch.tensor(placement.vbase, **i32)
+        self.v_rank = torch.tensor(placement.v_rank, **i32)
+        caps = [int(plan.local_rows[r].sum()) for r in range(world)]
+        self.capacity_rows = caps
+        self.capacity = torch.tensor(caps, **i32)
+        self.ids_global = torch.zeros(self.a_global, **i32)
+        self.route_global = MoeRouter(self.a_global, self.experts, dev)
+        self.v_plo = torch.zeros(self.V, **i32)
+        self.v_size = torch.zeros(self.V, **i32)
+        self.v_lbase = torch.zeros(self.V, **i32)
+        self.loffs = torch.zeros(self.n_local + 1, **i32)
+        self.rank_rows = torch.zeros(world, **i32)
+        cap_me = max(caps[rank], 1)
+        self.rowmap = torch.zeros(cap_me, **i32)
+        dt = local_weights.dtype
+        self.x_packed = torch.zeros(cap_me, self.k, device=dev, dtype=dt)
+        self.out = torch.zeros(self.a_local, self.n, device=dev, dtype=dt)
+        self.barrier_word = torch.zeros(1, **i32)
+        self._peer_bases = {}
+        if exchange:
+            self.set_peer_pointers(*self._exchange_pointers(lib))
+
+    def set_peer_pointers(self, xpk, outs):
+        """Per-rank device pointers of the packed-input and output buffers."""
+        if len(xpk) != self.world or len(outs) != self.world:
+            raise ValueError("one pointer per rank")
+        self.xpk_ptrs = _ptr_array(xpk, self.device)
+        self.out_ptrs = _ptr_array(outs, self.device)
+
+    def _exchange_pointers(self, lib):
+        """Per-rank device pointers of every rank's packed and output buffers."""
+        import torch.distributed as dist
+
+        mine = []
+        for t in (self.x_packed, self.out):
+            handle = ctypes.create_string_buffer(64)
+            offset = ctypes.c_int64(0)
+            if self.world > 1:
+                _native.check(lib.bokt_ipc_export(t.data_ptr(), handle, ctypes.byref(offset)),
+                              "bokt_ipc_export")
+            mine.append((bytes(handle.raw), int(offset.value)))
+        every = [None] * self.world
+        if self.world > 1:
+            dist.all_gather_object(every, mine, group=self.group)
+        else:
+            every = [mine]
+        xpk, outs = [], []
+        for r in range(self.world):
+            ptrs = []
+            for i, t in enumerate((self.x_packed, self.out)):
+                if r == self.rank:
+                    ptrs.append(t.data_ptr())
+                    continue
+                handle, offset = every[r][i]
+                base = self._peer_bases.get(handle)
+                if base is None:  # open each peer allocation once
+                    b, p = ctypes.c_void_p(), ctypes.c_void_p()
+                    _native.check(lib.bokt_ipc_import(handle, 0, ctypes.byref(b),
+                                                      ctypes.byref(p)), "bokt_ipc_import")
+                    base = self._peer_bases[handle] = b.value
+                ptrs.append(base + offset)
+            xpk.append(ptrs[0])
+            outs.append(ptrs[1])
+        return xpk, outs
+
+    def close(self):
+        """Unmap the peers' buffers (after the last step has completed everywhere)."""
+        lib = _native.load()
+        for base in self._peer_bases.values():
+            lib.bokt_ipc_close(base)
+        self._peer_bases = {}
+
+    def _barrier(self):
+        import torch.distributed as dist
+
+        if self.world > 1:
+            dist.all_reduce(self.barrier_word, group=self.group)
+
+    def _all_gather_ids(self, ids_local):
+        import torch.distributed as dist
+
+        if self.world == 1:
+            self.ids_global.copy_(ids_local.reshape(-1))
+        else:
+            dist.all_gather_into_tensor(self.ids_global, ids_local.reshape(-1), group=self.group)
+
+    def layout(self):
+        """Global routing, per-step layout and this rank's row map."""
+        lib = _native.load()
+        stream = _native.current_stream(self.device)
+        g = self.route_global(self.ids_global)
+        _native.check(lib.bokt_ep_plan(
+            g.counts.data_ptr(), g.offsets.data_ptr(), self.replicas.data_ptr(), self.experts,
+            self.v_rank.data_ptr(), self.V, self.world, self.rank, self.capacity.data_ptr(),
+            self.v_plo.data_ptr(), self.v_size.data_ptr(), self.v_lbase.data_ptr(),
+            self.loffs.data_ptr(), self.rank_rows.data_ptr(), stream), "bokt_ep_plan")
+        _native.check(lib.bokt_ep_rowmap(
+            g.perm.data_ptr(), self.ids_global.data_ptr(), g.offsets.data_ptr(),
+            g.counts.data_ptr(), self.replicas.data_ptr(), self.vbase.data_ptr(),
+            self.v_rank.data_ptr(), self.v_plo.data_ptr(), self.v_lbase.data_ptr(),
+            self.a_global, self.experts, self.rank, self.capacity_rows[self.rank],
+            self.rowmap.data_ptr(), stream), "bokt_ep_rowmap")
+
+    def dispatch(self, x_local):
+        lib = _native.load()
+        g = self.route_global
+        _native.check(lib.bokt_ep_dispatch(
+            x_local.data_ptr(), self.k, x_local.element_size(), self.ids_global.data_ptr(),
+            g.inv_perm.data_ptr(), g.offsets.data_ptr(), g.counts.data_ptr(),
+            self.replicas.data_ptr(), self.vbase.data_ptr(), self.v_rank.data_ptr(),
+            self.v_plo.data_ptr(), self.v_lbase.data_ptr(), self.xpk_ptrs.data_ptr(),
+            self.capacity.data_ptr(), self.a_local, self.topk, self.rank, self.experts,
+            _native.current_stream(self.device)), "bokt_ep_dispatch")
+
+    def compute_and_combine(self):
+        lib = _native.load()
+        rows = self.capacity_rows[self.rank]
+        if rows == 0:
+            return
+        _native.check(lib.bokt_moe_grouped_gemm_scatter(
+            self.x_packed.data_ptr(), self.w.data_ptr(), self.loffs.data_ptr(), 0, rows,
+            self.n_local, self.n, self.k, self.dtype, self.sm, self.rowmap.data_ptr(),
+            self.out_ptrs.data_ptr(), self.a_local, self.world, ctypes.byref(self.params),
+            _native.current_stream(self.device)), "bokt_moe_grouped_gemm_scatter")
+
+    def forward(self, x_local, ids_local):
+        """x_local [tokens_per_rank, K], ids_local [tokens_per_rank, topk] int32 ->
+        [tokens_per_rank * topk, N] (this rank's output buffer, overwritten by
+        the next step): row t*topk + k = x[t] @ W[ids[t, k]]."""
+        self._all_gather_ids(ids_local)
+        self.layout()
+        self.dispatch(x_local)
+        self._barrier()
+        self.compute_and_combine()
+        self._barrier()
+        return self.out

@@ -215,6 +215,70 @@ int bokt_ep_keys(const int32_t* perm, const int32_t* ids, const int32_t* offsets
 int bokt_check_counts(const int32_t* counts, const int32_t* expected, int n, int tag,
                       void* stream);
 
+/*
+ * Expert-parallel combine fused into the grouped GEMM: like
+ * bokt_moe_grouped_gemm, but packed output row l is not written to a local Y:
+ * with a = rowmap[l] and o = a / rows_per_owner it is stored at row
+ * a - o * rows_per_owner of out_ptrs[o] (a device array of `owners` pointers,
+ * each [rows_per_owner, N]; entries may be peer GPUs' buffers mapped through
+ * CUDA IPC, written with NVLink stores from the epilogue while later tiles
+ * compute).  tcgen05 path only.  No counterpart in the reference.
+ */
+int bokt_moe_grouped_gemm_scatter(const void* X, const void* W, const void* offsets,
+                                  int offsets_is_i64, int T, int E, int N, int K, int dtype,
+                                  int sm_count, const int32_t* rowmap, void* const* out_ptrs,
+                                  int rows_per_owner, int owners, const bokt_params* params,
+                                  void* stream);
+
+/*
+ * Per-step expert-parallel layout (one CTA): virtual expert v serves the
+ * global packed rows [v_plo[v], v_plo[v] + v_size[v]) and is stored at local
+ * rows [v_lbase[v], ...) of its rank's packed buffer (virtual experts in
+ * ascending v).  loffs: rank `me`'s grouped-GEMM offsets; rank_rows: rows per
+ * rank; a rank above capacity[r] sets the device status word (code 4).
+ * No counterpart in the reference.
+ */
+int bokt_ep_plan(const int32_t* counts, const int32_t* offsets, const int32_t* replicas, int E,
+                 const int32_t* v_rank, int V, int world, int me, const int32_t* capacity,
+                 int32_t* v_plo, int32_t* v_size, int32_t* v_lbase, int32_t* loffs,
+                 int32_t* rank_rows, void* stream);
+
+/*
+ * Expert-parallel dispatch over NVLink: each of this rank's a_local
+ * assignments copies its token row (x_local row a_local_index / topk) into the
+ * packed buffer xpk_ptrs[d] of the serving rank d at its local position
+ * (xpk_ptrs: device array of per-rank pointers, peers' buffers mapped through
+ * CUDA IPC).  Rows must be 16-byte multiples.  Positions beyond capacity[d]
+ * are reported (code 4) and skipped.  No counterpart in the reference.
+ */
+int bokt_ep_dispatch(const void* x_local, int cols, int elem_bytes, const int32_t* ids,
+                     const int32_t* inv_perm, const int32_t* offsets, const int32_t* counts,
+                     const int32_t* replicas, const int32_t* vbase, const int32_t* v_rank,
+                     const int32_t* v_plo, const int32_t* v_lbase, void* const* xpk_ptrs,
+                     const int32_t* capacity, int a_local, int topk, int me, int E,
+                     void* stream);
+
+/*
+ * rowmap[l] = global assignment index of local packed row l of rank `me`
+ * (input of the scatter epilogue).  No counterpart in the reference.
+ */
+int bokt_ep_rowmap(const int32_t* perm, const int32_t* ids, const int32_t* offsets,
+                   const int32_t* counts, const int32_t* replicas, const int32_t* vbase,
+                   const int32_t* v_rank, const int32_t* v_plo, const int32_t* v_lbase, int A,
+                   int E, int me, int capacity, int32_t* rowmap, void* stream);
+
+/*
+ * CUDA IPC plumbing for the expert-parallel peer buffers.  bokt_ipc_export
+ * writes the 64-byte IPC handle of the allocation containing `ptr` and the
+ * offset of `ptr` inside it (works for sub-allocations of a caching
+ * allocator); bokt_ipc_import opens a peer process's handle on the current
+ * device (peer access enabled lazily) and returns the mapping base (for
+ * bokt_ipc_close) and base + offset.  No counterpart in the reference.
+ */
+int bokt_ipc_export(const void* ptr, void* handle_out, int64_t* offset_out);
+int bokt_ipc_import(const void* handle, int64_t offset, void** base_out, void** ptr_out);
+int bokt_ipc_close(void* base);
+
 /* Resource usage of the kernel a call with these arguments would launch. */
 int bokt_kernel_attrs(int kernel, int dtype, int n, int k, const bokt_params* params,
                       bokt_attrs* out);

@@ -47,12 +47,24 @@ def main():
     a = np.arange(rank * tpr * 2, (rank + 1) * tpr * 2)
     ref = np.einsum("ak,akn->an", x.float().numpy()[a // 2], w.float().numpy()[ids[a]])
     stats = numerics.check_output(out.float().cpu().numpy(), ref, "bf16")
-    ok = torch.tensor([1 if code == 0 else 0], device=device)
+    # Peer-memory path (CUDA IPC + NVLink stores, one-word NCCL barriers).
+    pm = ep.PeerExpertParallelMoE(lw, placement, plan, rank, world, 2, tpr)
+    for _ in range(2):
+        pout = pm.forward(x[rank * tpr:(rank + 1) * tpr].to(device), ids_local)
+    torch.cuda.synchronize()
+    code2, _ = _native.device_status(reset=True)
+    pstats = numerics.check_output(pout.float().cpu().numpy(), ref, "bf16")
+    same = bool(torch.equal(pout, out))
+    dist.barrier()
+    pm.close()
+    code = code or code2
+    ok = torch.tensor([1 if code == 0 and same else 0], device=device)
     dist.all_reduce(ok, op=dist.ReduceOp.MIN)
     dist.barrier()
     dist.destroy_process_group()
     if rank == 0 and ok.item() == 1:
-        print(f"EP_NCCL_OK rel={stats['normwise_rel_error']:.2e}")
+        print(f"EP_NCCL_OK rel={stats['normwise_rel_error']:.2e} "
+              f"peer rel={pstats['normwise_rel_error']:.2e} identical={same}")
     return 0 if code == 0 else 1
 
 

@@ -75,3 +75,20 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.delenv("BOKT_LIBRARY")
     monkeypatch.setattr(_native, "_lib", None)
     assert _native.load() is not None
+
+
+def declared_arities():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    out = {}
+    for name, params in re.findall(r"\b(bokt_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", text):
+        params = params.strip()
+        out[name] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_ctypes_signatures_match_header_arity():
+    """Every ctypes binding passes exactly as many arguments as the C declaration."""
+    arities = declared_arities()
+    assert arities, "no declarations parsed"
+    for name, n in arities.items():
+        assert len(_native.SIGNATURES[name][1]) == n, (name, n, len(_native.SIGNATURES[name][1]))

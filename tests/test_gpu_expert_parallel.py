@@ -136,3 +136,64 @@ def test_nccl_two_ranks(cuda_device):
                          text=True, cwd=REPO)
     assert run.returncode == 0, run.stdout[-3000:] + run.stderr[-3000:]
     assert "EP_NCCL_OK" in run.stdout
+
+
+def build_peer_ranks(world, tokens, experts, k, n, seed, device):
+    ids_cpu = zipf_routing(tokens, experts, 2, 1.1, seed).reshape(-1)
+    ids = ids_cpu.numpy()
+    placement = ep.plan_placement(np.bincount(ids, minlength=experts), world)
+    tpr = tokens // world
+    plan = ep.plan_splits(ids, placement, 2, tpr)
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(tokens, k, generator=g).bfloat16()
+    w = (0.05 * torch.randn(experts, k, n, generator=g)).bfloat16()
+    wd = w.to(device)
+    ranks = [ep.PeerExpertParallelMoE(wd[ep.local_weight_slices(placement, r)].contiguous(),
+                                      placement, plan, r, world, 2, tpr, exchange=False)
+             for r in range(world)]
+    xpk = [m.x_packed.data_ptr() for m in ranks]
+    outs = [m.out.data_ptr() for m in ranks]
+    for m in ranks:
+        m.set_peer_pointers(xpk, outs)
+    return ids_cpu, ids, x, w, placement, ranks
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_peer_path_virtual_ranks_on_one_gpu(world, cuda_device):
+    """Dispatch stores and the scatter epilogue write into other ranks' buffers
+    (here: other buffers of the same GPU); the result must equal the oracle."""
+    tokens, experts, k, n = 4096, 32, 256, 512
+    ids_cpu, ids, x, w, placement, ranks = build_peer_ranks(world, tokens, experts, k, n, 11,
+                                                            cuda_device)
+    _native.device_status(reset=True)
+    tpr = tokens // world
+    ids_dev = ids_cpu.to(cuda_device).to(torch.int32)
+    xd = x.to(cuda_device)
+    for r, m in enumerate(ranks):
+        m.out.fill_(float("nan"))
+        m.ids_global.copy_(ids_dev)
+        m.layout()
+    for r, m in enumerate(ranks):
+        m.dispatch(xd[r * tpr:(r + 1) * tpr])
+    for m in ranks:
+        m.compute_and_combine()
+    torch.cuda.synchronize()
+    assert _native.device_status(reset=True)[0] == 0
+    xf, wf = as_f32(x), as_f32(w)
+    for r, m in enumerate(ranks):
+        assert m.rank_rows.cpu().tolist() == [int(v) for v in placement.rank_rows]
+        a = np.arange(r * tpr * 2, (r + 1) * tpr * 2)
+        ref = np.einsum("ak,akn->an", xf[a // 2], wf[ids[a]])
+        gate(m.out, ref, "bf16")
+
+
+def test_peer_path_single_rank_forward(cuda_device):
+    tokens, experts, k, n = 2048, 16, 128, 256
+    ids_cpu, ids, x, w, placement, ranks = build_peer_ranks(1, tokens, experts, k, n, 12,
+                                                            cuda_device)
+    m = ranks[0]
+    for _ in range(2):
+        out = m.forward(x.to(cuda_device), ids_cpu.to(cuda_device).to(torch.int32))
+    torch.cuda.synchronize()
+    a = np.arange(tokens * 2)
+    gate(out, np.einsum("ak,akn->an", as_f32(x)[a // 2], as_f32(w)[ids[a]]), "bf16")
