@@ -12,7 +12,13 @@ kernels:
   warp-specialised CTA (TMA + MMA + 4 epilogue warps = 6); ``GROUP_M`` the
   grouped-M raster of the dense GEMM; ``CTA_MULTIPLIER`` the persistent grid
   of the grouped GEMM (``sm_count * CTA_MULTIPLIER``).
-* RMSNorm: ``ROWS_PER_CTA`` and ``num_warps`` as in the reference.
+* GEMM only: ``CTA_GROUP`` 1 (one CTA per 128-row tile) or 2 (CTA pairs on two
+  SMs, tcgen05 cta_group::2, 256-row tiles).
+* RMSNorm: ``ROWS_PER_CTA`` and ``num_warps`` as in the reference, plus
+  ``num_stages``: 1 keeps the reference's one-row-slice-per-CTA shape;
+  2 or more selects the persistent kernel in which a producer warp streams
+  rows into a ring of that many shared-memory row buffers (cp.async.bulk) and
+  ``num_warps`` consumer warps normalise one row each.
 """
 
 from dataclasses import asdict, dataclass
@@ -67,6 +73,7 @@ def search_space(kernel: str, profile: str = "full") -> dict[str, list[int]]:
         return {
             "ROWS_PER_CTA": [1, 2, 4, 8] if profile == "full" else [1, 2],
             "num_warps": [1, 2, 4, 8, 16] if profile == "full" else [4, 8],
+            "num_stages": [1, 4, 8, 16] if profile == "full" else [1, 8],
         }
     space = {
         "BLOCK_M": [128],
@@ -85,6 +92,8 @@ def search_space(kernel: str, profile: str = "full") -> dict[str, list[int]]:
         }
     if kernel == "gemm":
         space["GROUP_M"] = [1, 4, 8, 16] if profile == "full" else [1, 4]
+        if profile == "full":
+            space["CTA_GROUP"] = [1, 2]
     else:
         space["CTA_MULTIPLIER"] = [1, 2, 4] if profile == "full" else [1, 2]
     return space
@@ -93,10 +102,10 @@ def search_space(kernel: str, profile: str = "full") -> dict[str, list[int]]:
 def default_params(kernel: str) -> dict[str, int]:
     """A good starting point on B200 (used by bench.py and as a tuning seed)."""
     if kernel == "rmsnorm":
-        return {"ROWS_PER_CTA": 1, "num_warps": 4}
+        return {"ROWS_PER_CTA": 1, "num_warps": 4, "num_stages": 1}
     p = {"BLOCK_M": 128, "BLOCK_N": 256, "BLOCK_K": 64, "num_warps": 6, "num_stages": 4}
     if kernel == "gemm":
-        p["GROUP_M"] = 8
+        p.update(GROUP_M=8, CTA_GROUP=2, num_stages=6)
     else:
         p["CTA_MULTIPLIER"] = 1
     return p

@@ -14,6 +14,7 @@
 #include "bokt_device.cuh"
 #include "gemm_simt.cuh"
 #include "gemm_tc.cuh"
+#include "gemm_tc2.cuh"
 #include "moe_route.cuh"
 #include "rmsnorm.cuh"
 
@@ -199,7 +200,7 @@ const void* tc_kernel(bool grouped, int dtype, int bn, bool scatter = false) {
 }
 
 struct TcConfig {
-  int bn, stages, group_m, smem;
+  int bn, stages, group_m, smem, cta_group;
 };
 
 int resolve_tc_config(const bokt_params* p, bool grouped, int experts, int smem_optin,
@@ -216,10 +217,16 @@ int resolve_tc_config(const bokt_params* p, bool grouped, int experts, int smem_
     return fail(BOKT_ERR_CONFIG, "block_n must be 64, 128 or 256 (got %d)", bn);
   if (warps != 6) return fail(BOKT_ERR_CONFIG, "num_warps must be 6 (TMA, MMA, 4 epilogue)");
   if (p->split_k > 1) return fail(BOKT_ERR_UNSUPPORTED, "split_k > 1 is not implemented");
-  if (p->cta_group > 1) return fail(BOKT_ERR_UNSUPPORTED, "cta_group 2 is not implemented");
-  const int stages = param_or(p->stages, bn == 256 ? 4 : 6);
+  const int cta_group = param_or(p->cta_group, 1);
+  if (cta_group != 1 && cta_group != 2) return fail(BOKT_ERR_CONFIG, "cta_group must be 1 or 2");
+  if (cta_group == 2 && grouped)
+    return fail(BOKT_ERR_UNSUPPORTED, "cta_group 2 is implemented for the dense GEMM only");
+  if (cta_group == 2 && bn == 64)
+    return fail(BOKT_ERR_CONFIG, "cta_group 2 needs block_n 128 or 256");
+  const int stages = param_or(p->stages, cta_group == 2 ? (bn == 256 ? 6 : 8) : (bn == 256 ? 4 : 6));
   if (stages < 2 || stages > 8) return fail(BOKT_ERR_CONFIG, "stages must be in [2, 8]");
-  int smem = bokt::gemm_tc_smem_bytes(bn, stages, grouped, experts);
+  int smem = cta_group == 2 ? bokt::gemm_tc2_smem_bytes(bn, stages)
+                            : bokt::gemm_tc_smem_bytes(bn, stages, grouped, experts);
   if (smem > smem_optin)
     return fail(BOKT_ERR_CONFIG, "block_n=%d stages=%d needs %d bytes of shared memory (max %d)",
                 bn, stages, smem, smem_optin);
@@ -231,6 +238,36 @@ int resolve_tc_config(const bokt_params* p, bool grouped, int experts, int smem_
   out->stages = stages;
   out->group_m = param_or(p->group_m, 8);
   out->smem = smem;
+  out->cta_group = cta_group;
+  return BOKT_OK;
+}
+
+const void* tc2_kernel(int dtype, int bn) {
+  if (dtype == BOKT_BF16)
+    return bn == 256 ? reinterpret_cast<const void*>(&bokt::gemm_tc2_kernel<256, __nv_bfloat16>)
+                     : reinterpret_cast<const void*>(&bokt::gemm_tc2_kernel<128, __nv_bfloat16>);
+  return bn == 256 ? reinterpret_cast<const void*>(&bokt::gemm_tc2_kernel<256, __half>)
+                   : reinterpret_cast<const void*>(&bokt::gemm_tc2_kernel<128, __half>);
+}
+
+// Dense GEMM on CTA pairs: cluster of 2 along x, PDL as every other launch.
+int launch_tc2(int dtype, const TcConfig& cfg, const CUtensorMap& ma, const CUtensorMap& mb,
+               const GemmTcArgs& args, int pairs, cudaStream_t s) {
+  const void* fn = tc2_kernel(dtype, cfg.bn);
+  int rc = ensure_smem(fn, cfg.smem);
+  if (rc) return rc;
+  void* kargs[] = {const_cast<CUtensorMap*>(&ma), const_cast<CUtensorMap*>(&mb),
+                   const_cast<GemmTcArgs*>(&args)};
+  cudaLaunchAttribute attr[2];
+  cudaLaunchConfig_t lc = launch_config(dim3(2 * pairs), dim3(bokt::kGemmThreads), cfg.smem, s,
+                                        attr);
+  attr[lc.numAttrs].id = cudaLaunchAttributeClusterDimension;
+  attr[lc.numAttrs].val.clusterDim.x = 2;
+  attr[lc.numAttrs].val.clusterDim.y = 1;
+  attr[lc.numAttrs].val.clusterDim.z = 1;
+  lc.numAttrs += 1;
+  cudaError_t e = cudaLaunchKernelExC(&lc, fn, kargs);
+  if (e != cudaSuccess) return cuda_fail(e, "gemm_tc2 launch");
   return BOKT_OK;
 }
 
@@ -265,6 +302,7 @@ bool tc_eligible(const void* A, const void* B, const void* C, int N, int K) {
 // ----------------------------------------------------------------- RMSNorm dispatch
 struct NormConfig {
   int rows_per_cta, threads, tpr_log2, vpt;  // vpt 0 = generic kernel
+  int ring_slots;                            // > 0: persistent TMA-staged ring kernel
 };
 
 int resolve_norm_config(const bokt_params* p, int N, bool vec_ok, NormConfig* out) {
@@ -289,7 +327,22 @@ int resolve_norm_config(const bokt_params* p, int N, bool vec_ok, NormConfig* ou
     while (v < need) v <<= 1;
     if (v <= 16) vpt = v;
   }
-  *out = {rows, threads, lg, vpt};
+  const int stages = param_or(p->stages, 1);
+  if (stages < 1 || stages > 32) return fail(BOKT_ERR_CONFIG, "stages must be in [1, 32]");
+  // The ring kernel streams whole rows with cp.async.bulk (16-byte multiples,
+  // 16-byte aligned); odd or unaligned rows take the per-row kernels instead,
+  // as odd GEMM shapes take the SIMT edge path.
+  int ring = 0;
+  if (stages >= 2 && vec_ok) {
+    if (warps > 31) return fail(BOKT_ERR_CONFIG, "ring kernel: num_warps must be <= 31");
+    if (stages % warps != 0)
+      return fail(BOKT_ERR_CONFIG,
+                  "ring kernel: stages (%d) must be a multiple of num_warps (%d) so each ring "
+                  "slot is consumed by one warp",
+                  stages, warps);
+    ring = stages;
+  }
+  *out = {rows, threads, lg, vpt, ring};
   return BOKT_OK;
 }
 
@@ -372,6 +425,13 @@ int bokt_gemm(const void* A, const void* B, void* C, int M, int N, int K, int dt
   args.K = K;
   args.group_m = cfg.group_m;
   args.stages = cfg.stages;
+  if (cfg.cta_group == 2) {
+    args.idesc = bokt::make_idesc_f16(uint32_t(dtype), 256, uint32_t(cfg.bn));
+    const long long tiles2 = (long long)((M + 255) / 256) * ((N + cfg.bn - 1) / cfg.bn);
+    const long long max_pairs = dev.sm_count / 2;
+    const int pairs = int(tiles2 < max_pairs ? tiles2 : max_pairs);
+    return launch_tc2(dtype, cfg, ma, mb, args, pairs, s);
+  }
   args.idesc = bokt::make_idesc_f16(uint32_t(dtype), 128, uint32_t(cfg.bn));
   const long long tiles = (long long)((M + 127) / 128) * ((N + cfg.bn - 1) / cfg.bn);
   const int grid = int(tiles < dev.sm_count ? tiles : dev.sm_count);
@@ -555,6 +615,31 @@ int bokt_rmsnorm(const void* X, const void* W, void* Y, int M, int N, float eps,
   NormConfig cfg;
   int rc = resolve_norm_config(params, N, vec_ok, &cfg);
   if (rc) return rc;
+  if (cfg.ring_slots > 0) {
+    DeviceInfo dev;
+    rc = device_info(&dev);
+    if (rc) return rc;
+    const int smem = bokt::rmsnorm_ring_smem_bytes(N, 2, cfg.ring_slots);
+    if (smem > dev.smem_optin)
+      return fail(BOKT_ERR_CONFIG, "ring kernel: %d slots of %d-element rows need %d bytes of "
+                                   "shared memory (max %d)", cfg.ring_slots, N, smem,
+                  dev.smem_optin);
+    const void* rfn = dtype == BOKT_BF16
+                          ? reinterpret_cast<const void*>(&bokt::rmsnorm_ring_kernel<__nv_bfloat16>)
+                          : reinterpret_cast<const void*>(&bokt::rmsnorm_ring_kernel<__half>);
+    rc = ensure_smem(rfn, smem);
+    if (rc) return rc;
+    int per_sm = (228 * 1024) / (smem + 1024);
+    if (per_sm < 1) per_sm = 1;
+    if (per_sm > 4) per_sm = 4;
+    long long grid = (long long)dev.sm_count * per_sm;
+    if (grid > M) grid = M;
+    int slots = cfg.ring_slots;
+    void* rargs[] = {const_cast<void**>(&X), const_cast<void**>(&W), &Y, &M, &N, &eps, &slots};
+    cudaError_t e = launch_ptr(rfn, dim3(unsigned(grid)), dim3(cfg.threads + 32), smem, s, rargs);
+    if (e != cudaSuccess) return cuda_fail(e, "rmsnorm ring launch");
+    return BOKT_OK;
+  }
   const int grid = (M + cfg.rows_per_cta - 1) / cfg.rows_per_cta;
   const void* fn = dtype == BOKT_BF16 ? norm_kernel<__nv_bfloat16>(cfg.vpt)
                                       : norm_kernel<__half>(cfg.vpt);
@@ -738,7 +823,7 @@ int bokt_kernel_attrs(int kernel, int dtype, int n, int k, const bokt_params* pa
       TcConfig cfg;
       rc = resolve_tc_config(params, grouped, grouped ? 64 : 0, dev.smem_optin, &cfg);
       if (rc) return rc;
-      fn = tc_kernel(grouped, dtype, cfg.bn);
+      fn = cfg.cta_group == 2 ? tc2_kernel(dtype, cfg.bn) : tc_kernel(grouped, dtype, cfg.bn);
       dyn = cfg.smem;
       threads = bokt::kGemmThreads;
       path = 0;
@@ -752,9 +837,18 @@ int bokt_kernel_attrs(int kernel, int dtype, int n, int k, const bokt_params* pa
     NormConfig cfg;
     rc = resolve_norm_config(params, n, (n % 8) == 0, &cfg);
     if (rc) return rc;
-    fn = dtype == BOKT_BF16 ? norm_kernel<__nv_bfloat16>(cfg.vpt) : norm_kernel<__half>(cfg.vpt);
-    threads = cfg.threads;
-    path = cfg.vpt ? 2 : 3;
+    if (cfg.ring_slots > 0) {
+      fn = dtype == BOKT_BF16
+               ? reinterpret_cast<const void*>(&bokt::rmsnorm_ring_kernel<__nv_bfloat16>)
+               : reinterpret_cast<const void*>(&bokt::rmsnorm_ring_kernel<__half>);
+      threads = cfg.threads + 32;
+      dyn = bokt::rmsnorm_ring_smem_bytes(n, 2, cfg.ring_slots);
+      path = 4;
+    } else {
+      fn = dtype == BOKT_BF16 ? norm_kernel<__nv_bfloat16>(cfg.vpt) : norm_kernel<__half>(cfg.vpt);
+      threads = cfg.threads;
+      path = cfg.vpt ? 2 : 3;
+    }
   } else {
     return fail(BOKT_ERR_INVALID, "unknown kernel id %d", kernel);
   }

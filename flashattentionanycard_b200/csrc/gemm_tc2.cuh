@@ -1,0 +1,228 @@
+// Dense GEMM on CTA pairs (cluster of 2, tcgen05 cta_group::2), sm_100a.
+//
+// Same contract as the dense path of gemm_tc.cuh (kernels/gemm.py:7-40 of the
+// reference: C = A * B, row-major, GROUP_M raster, masked edges), with
+// 256 x BN tiles computed by a pair of CTAs on two SMs:
+//   * CTA r of the pair stages rows [m0 + 128 r, +128) of A and columns
+//     [n0 + r BN/2, +BN/2) of B, each with its own TMA loads (no cross-CTA
+//     copies); both CTAs' loads complete on the leader's (r = 0) barrier;
+//   * the leader issues tcgen05.mma.cta_group::2 (M = 256, N = BN, K = 16),
+//     which reads both CTAs' shared memory and accumulates 128 rows x BN
+//     columns in each CTA's TMEM;
+//   * the leader's commits free both CTAs' stages and hand both CTAs'
+//     accumulators to their epilogues; each epilogue warp arrives on the
+//     leader's accumulator-empty barrier.
+// Per SM the MMA reads 8 KB of operands per 128 x 256 x 16 step instead of
+// 12 KB, and a stage is 32 KB (BN = 256), so the ring is 6 deep.
+#pragma once
+
+#include "bokt_device.cuh"
+#include "gemm_tc.cuh"
+
+namespace bokt {
+
+template <int BN>
+struct GemmTc2Shape {
+  static constexpr int kBHalf = BN / 2;
+  static constexpr int kBBytes = kBHalf * kGemmBK * 2;
+  static constexpr int kStageBytes = kGemmABytes + kBBytes;
+  static constexpr int kTmemCols = 2 * BN;
+  static_assert(BN == 128 || BN == 256, "pair tiles need BN of 128 or 256");
+};
+
+__host__ __device__ inline int gemm_tc2_smem_bytes(int bn, int stages) {
+  return 1024 + stages * (kGemmABytes + (bn / 2) * kGemmBK * 2) + (2 * stages + 4) * 8 + 16;
+}
+
+template <int BN, typename OutT>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    GemmTcArgs args) {
+  using Shape = GemmTc2Shape<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+
+  const int stages = args.stages;
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + stages * kGemmABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + stages * Shape::kBBytes);
+  uint64_t* empty = full + stages;
+  uint64_t* tfull = empty + stages;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+  const int M = args.M, N = args.N;
+  const int nm = (M + 2 * kGemmBM - 1) / (2 * kGemmBM);
+  const int nn = (N + BN - 1) / BN;
+  const int ntiles = nm * nn;
+  const int nkb = (args.K + kGemmBK - 1) / kGemmBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * 4);  // one arrival per epilogue warp of both CTAs
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_holder, Shape::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  pdl_allow_next();
+  pdl_wait();
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  // 256-row tiles, GROUP_M raster as kernels/gemm.py:20-26.
+  auto tile_at = [&](int t, int& m0, int& n0) {
+    const int per_group = args.group_m * nn;
+    const int group = t / per_group;
+    const int first_m = group * args.group_m;
+    const int gm = min(nm - first_m, args.group_m);
+    const int local = t - group * per_group;
+    m0 = (first_m + local % gm) * 2 * kGemmBM;
+    n0 = (local / gm) * BN;
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producers (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = pair; t < ntiles && ok; t += npairs) {
+        int m0, n0;
+        tile_at(t, m0, n0);
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, abort_flag, 11)) {
+            ok = false;
+            break;
+          }
+          const uint32_t full_leader = map_shared(smem_addr(&full[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * Shape::kStageBytes);
+          tma_load_2d_pair(sA + stage * kGemmABytes, &tmA, full_leader, kb * kGemmBK,
+                           m0 + static_cast<int>(rank) * kGemmBM);
+#pragma unroll
+          for (int c = 0; c < Shape::kBHalf / 64; ++c)
+            tma_load_2d_pair(sB + stage * Shape::kBBytes + c * 8192, &tmB, full_leader,
+                             n0 + static_cast<int>(rank) * Shape::kBHalf + c * 64, kb * kGemmBK);
+          if (++stage == stages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (leader && lane == 0) {
+      const uint32_t idesc = args.idesc;
+      int stage = 0;
+      uint32_t phase = 0;
+      int i = 0;
+      bool ok = true;
+      for (int t = pair; t < ntiles && ok; t += npairs, ++i) {
+        const int acc = i & 1;
+        const uint32_t acc_phase = (static_cast<uint32_t>(i) >> 1) & 1u;
+        if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, abort_flag, 12)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait_cluster(&full[stage], phase, abort_flag, 13)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_addr(sA + stage * kGemmABytes);
+          const uint32_t b_addr = smem_addr(sB + stage * Shape::kBBytes);
+#pragma unroll
+          for (int k = 0; k < kGemmBK / 16; ++k) {
+            const uint64_t a_desc = smem_desc_sw128(a_addr + k * 32, 16, 1024);
+            const uint64_t b_desc = smem_desc_sw128(b_addr + k * 2048, 64 * 128, 1024);
+            umma_f16_ss_pair(d_tmem, a_desc, b_desc, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit_both(&empty[stage]);
+          if (++stage == stages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_both(&tfull[acc]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    OutT* C = reinterpret_cast<OutT*>(args.C);
+    int i = 0;
+    for (int t = pair; t < ntiles; t += npairs, ++i) {
+      int m0, n0;
+      tile_at(t, m0, n0);
+      const int acc = i & 1;
+      const uint32_t acc_phase = (static_cast<uint32_t>(i) >> 1) & 1u;
+      const bool ok = mbar_wait_cluster(&tfull[acc], acc_phase, abort_flag, 14);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const uint32_t taddr =
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      const int row = m0 + static_cast<int>(rank) * kGemmBM + r;
+      const bool row_ok = row < M;
+      OutT* crow = C + static_cast<size_t>(row_ok ? row : 0) * N + n0;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c), v);
+        tmem_ld_wait();
+        if (row_ok) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            if (n0 + c + j < N) {
+              uint4 pk;
+              pk.x = Pack2<OutT>::pack(__uint_as_float(v[j + 0]), __uint_as_float(v[j + 1]));
+              pk.y = Pack2<OutT>::pack(__uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+              pk.z = Pack2<OutT>::pack(__uint_as_float(v[j + 4]), __uint_as_float(v[j + 5]));
+              pk.w = Pack2<OutT>::pack(__uint_as_float(v[j + 6]), __uint_as_float(v[j + 7]));
+              *reinterpret_cast<uint4*>(crow + c + j) = pk;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(map_shared(smem_addr(&tempty[acc]), 0));
+    }
+  }
+
+  // ---------------------------------------------------------------- teardown
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its peer may still signal its barriers
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Shape::kTmemCols);
+  }
+}
+
+}  // namespace bokt

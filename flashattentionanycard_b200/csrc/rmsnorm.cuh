@@ -122,3 +122,126 @@ __global__ void rmsnorm_generic_kernel(const T* __restrict__ X, const T* __restr
 }
 
 }  // namespace bokt
+
+namespace bokt {
+
+// Persistent TMA-staged RMSNorm (N % 8 == 0, 16-byte aligned rows).
+//   grid: one CTA per SM; CTA c handles rows c, c + grid, c + 2 grid, ...
+//   warp `consumers` (the last): producer; its lane 0 streams whole rows into
+//     a ring of `slots` row buffers with cp.async.bulk (one mbarrier per slot)
+//   warps 0 .. consumers-1: consumer w takes the CTA's rows w, w + consumers,
+//     ...: sum of squares from shared memory (warp shuffles only), then
+//     y = (x * r) * w with w staged once per CTA in shared memory, 16-byte
+//     coalesced stores straight to HBM, then frees the slot.
+// Up to `slots` rows per SM are in flight regardless of how fast rows are
+// consumed, and no CTA-wide barrier sits on the per-row path.
+// slots must be a multiple of the consumer warps: then every use of a slot is
+// consumed by the same warp, in order, so a parity wait on the slot's barrier
+// can never be satisfied by the completion of an older use of the slot.  The
+// host enforces it.  Before the CTA exits, the producer also waits until every
+// copy it issued has landed.
+template <typename T>
+__global__ void __launch_bounds__(1024, 1)
+    rmsnorm_ring_kernel(const T* __restrict__ X, const T* __restrict__ W, T* __restrict__ Y, int M,
+                        int N, float eps, int slots) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
+  const int row_bytes = N * static_cast<int>(sizeof(T));
+  const int nvec = row_bytes / 16;
+  uint4* w_s = reinterpret_cast<uint4*>(smem);
+  uint8_t* ring = smem + ((row_bytes + 127) & ~127);
+  const int slot_stride = (row_bytes + 127) & ~127;
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + static_cast<size_t>(slots) * slot_stride);
+  uint64_t* empty = full + slots;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + slots);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int consumers = (blockDim.x >> 5) - 1;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < slots; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  pdl_allow_next();
+  pdl_wait();
+  const uint4* wg = reinterpret_cast<const uint4*>(W);
+  for (int v = threadIdx.x; v < nvec; v += blockDim.x) w_s[v] = __ldg(wg + v);
+  __syncthreads();
+
+  const int my_rows = M > static_cast<int>(blockIdx.x)
+                          ? (M - static_cast<int>(blockIdx.x) + gridDim.x - 1) / gridDim.x
+                          : 0;
+  if (warp == consumers) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int k = 0; k < my_rows; ++k) {
+        const int s = k % slots;
+        const uint32_t phase = static_cast<uint32_t>(k / slots) & 1u;
+        if (!mbar_wait(&empty[s], phase ^ 1u, abort_flag, 21)) break;
+        const long long row = static_cast<long long>(blockIdx.x) + static_cast<long long>(k) * gridDim.x;
+        mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(row_bytes));
+        bulk_load(ring + static_cast<size_t>(s) * slot_stride, X + row * N,
+                  static_cast<uint32_t>(row_bytes), &full[s]);
+        ++issued;
+      }
+      // Every issued copy has landed before this CTA may exit (bounded waits).
+      for (int k = issued - slots > 0 ? issued - slots : 0; k < issued; ++k) {
+        const int s = k % slots;
+        const uint32_t phase = static_cast<uint32_t>(k / slots) & 1u;
+        if (!mbar_wait(&full[s], phase, abort_flag, 23)) break;
+      }
+    }
+  } else {
+    for (int k = warp; k < my_rows; k += consumers) {
+      const int s = k % slots;
+      const uint32_t phase = static_cast<uint32_t>(k / slots) & 1u;
+      const bool ok = mbar_wait(&full[s], phase, abort_flag, 22);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      const uint4* xs = reinterpret_cast<const uint4*>(ring + static_cast<size_t>(s) * slot_stride);
+      float ss = 0.f;
+      for (int v = lane; v < nvec; v += 32) {
+        const uint4 xv = xs[v];
+        const uint32_t* u = reinterpret_cast<const uint32_t*>(&xv);
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const float2 f = Pack2<T>::unpack(u[h]);
+          ss = fmaf(f.x, f.x, ss);
+          ss = fmaf(f.y, f.y, ss);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float scale = rsqrtf(ss / static_cast<float>(N) + eps);
+      const long long row = static_cast<long long>(blockIdx.x) + static_cast<long long>(k) * gridDim.x;
+      uint4* yr = reinterpret_cast<uint4*>(Y + row * N);
+      for (int v = lane; v < nvec; v += 32) {
+        const uint4 xv = xs[v];
+        const uint4 wv = w_s[v];
+        const uint32_t* xu = reinterpret_cast<const uint32_t*>(&xv);
+        const uint32_t* wu = reinterpret_cast<const uint32_t*>(&wv);
+        uint4 out;
+        uint32_t* ou = reinterpret_cast<uint32_t*>(&out);
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const float2 xf = Pack2<T>::unpack(xu[h]);
+          const float2 wf = Pack2<T>::unpack(wu[h]);
+          ou[h] = Pack2<T>::pack((xf.x * scale) * wf.x, (xf.y * scale) * wf.y);
+        }
+        yr[v] = out;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+  }
+}
+
+__host__ __device__ inline int rmsnorm_ring_smem_bytes(int n, int elem_bytes, int slots) {
+  const int row = ((n * elem_bytes) + 127) & ~127;
+  return 128 + row * (slots + 1) + slots * 16 + 16;
+}
+
+}  // namespace bokt

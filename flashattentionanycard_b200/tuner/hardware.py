@@ -117,17 +117,29 @@ def gemm_shared_bytes(block_n, stages, experts=0):
     return total
 
 
+def gemm_pair_shared_bytes(block_n, stages):
+    """Dynamic shared memory per CTA of the CTA-pair GEMM (csrc/gemm_tc2.cuh)."""
+    return 1024 + stages * (GEMM_BM * GEMM_BK * 2 + (block_n // 2) * GEMM_BK * 2) + (2 * stages + 4) * 8 + 16
+
+
+def rmsnorm_ring_bytes(columns, stages, elem_bytes=2):
+    """Dynamic shared memory of the ring RMSNorm (csrc/rmsnorm.cuh rmsnorm_ring_smem_bytes)."""
+    row = (columns * elem_bytes + 127) // 128 * 128
+    return 128 + row * (stages + 1) + stages * 16 + 16
+
+
 def resource_estimate(kernel, params, columns=0, experts=0):
     if kernel == "rmsnorm":
         threads = params["num_warps"] * 32
         rows = params["ROWS_PER_CTA"]
         per_row = max(threads // rows, 1)
         vectors = -(-(columns // 8) // per_row) if columns % 8 == 0 else 0
+        stages = params.get("num_stages", 1)
         return {
             "threads_per_row": per_row,
             "vectors_per_thread": vectors,
             "single_pass_registers": vectors <= 16 and columns % 8 == 0,
-            "shared_bytes_estimate": 128,
+            "shared_bytes_estimate": rmsnorm_ring_bytes(columns, stages) if stages >= 2 else 128,
         }
     return {
         "shared_bytes_estimate": gemm_shared_bytes(params["BLOCK_N"], params["num_stages"], experts),
@@ -146,6 +158,13 @@ def prune_reason(hardware, kernel, params, columns=0, heuristic_smem=False):
     if kernel == "rmsnorm":
         if params["ROWS_PER_CTA"] > warps * hardware.warp_size:
             return "rmsnorm_implementation_limit"
+        stages = params.get("num_stages", 1)
+        if stages >= 2 and columns % 8 == 0:
+            # Ring kernel: each ring slot must always be consumed by the same warp.
+            if stages % warps or (warps + 1) * hardware.warp_size > hardware.max_threads_per_block:
+                return "rmsnorm_implementation_limit"
+            if rmsnorm_ring_bytes(columns, stages) > hardware.shared_memory_per_block:
+                return "shared_memory_exceeds_device_limit"
         return None
     if warps != GEMM_WARPS:
         return "illegal_threads_per_block"
@@ -153,8 +172,12 @@ def prune_reason(hardware, kernel, params, columns=0, heuristic_smem=False):
         return "illegal_tile_shape"
     if params["BLOCK_N"] not in (64, 128, 256) or 2 * params["BLOCK_N"] > TMEM_COLUMNS:
         return "illegal_tile_shape"
+    pair = params.get("CTA_GROUP", 1) == 2
+    if pair and (kernel != "gemm" or params["BLOCK_N"] == 64):
+        return "illegal_tile_shape"
     experts = 64 if kernel == "moe_grouped_gemm" else 0
-    smem = gemm_shared_bytes(params["BLOCK_N"], params["num_stages"], experts)
+    smem = (gemm_pair_shared_bytes(params["BLOCK_N"], params["num_stages"]) if pair
+            else gemm_shared_bytes(params["BLOCK_N"], params["num_stages"], experts))
     if smem > hardware.shared_memory_per_block:
         return "shared_memory_exceeds_device_limit"
     if heuristic_smem and smem > 0.85 * hardware.shared_memory_per_block:

@@ -63,7 +63,9 @@ extern "C" {
  *                         (grouped-M raster width), cta_multiplier (grouped GEMM
  *                         persistent grid = sm_count * cta_multiplier),
  *                         num_warps (6: TMA, MMA and four epilogue warps)
- *   RMSNorm             : rows_per_cta, num_warps
+ *   RMSNorm             : rows_per_cta, num_warps; stages >= 2 selects the persistent
+ *                         ring kernel (stages row buffers, num_warps consumer warps)
+ *   GEMM                : cta_group 2 runs CTA pairs (tcgen05 cta_group::2, 256-row tiles)
  */
 typedef struct bokt_params {
   int32_t block_m;
@@ -75,7 +77,7 @@ typedef struct bokt_params {
   int32_t num_warps;
   int32_t rows_per_cta;
   int32_t split_k;   /* reserved: must be 0 or 1 */
-  int32_t cta_group; /* reserved: must be 0 or 1 */
+  int32_t cta_group; /* 0/1: one CTA per tile; 2: CTA pairs (dense GEMM) */
   int32_t reserved[6];
 } bokt_params;
 
@@ -85,7 +87,7 @@ typedef struct bokt_attrs {
   int32_t local_bytes;    /* local memory per thread (spill indicator) */
   int32_t threads;        /* threads per CTA */
   int32_t max_threads;    /* cudaFuncAttributes.maxThreadsPerBlock */
-  int32_t path;           /* 0 = tcgen05/TMA, 1 = SIMT edge path, 2 = vector, 3 = scalar */
+  int32_t path;           /* 0 = tcgen05/TMA, 1 = SIMT edge, 2 = vector, 3 = scalar, 4 = ring */
 } bokt_attrs;
 
 /* ABI version and the sm architecture the library was built for (100). */

@@ -168,7 +168,10 @@ def test_rmsnorm_every_config(shape, dtype, cuda_device):
     w = (1 + 0.1 * torch.randn(n, generator=g)).to(worker_dtype(dtype))
     ref = numerics.rmsnorm_fp32(as_f32(x), as_f32(w), 1e-6)
     xd, wd = x.to(cuda_device), w.to(cuda_device)
+    hw = Hardware.detect(cuda_device.index)
     for p in grid_configs(search_space("rmsnorm")):
+        if prune_reason(hw, "rmsnorm", p, n):
+            continue
         out = nan_like((m, n), dtype, cuda_device)
         rmsnorm.launch(xd, wd, out, p, 1e-6)
         torch.cuda.synchronize()
@@ -265,3 +268,58 @@ def test_worker_evaluate_and_confirmation(kernel, dtype, cuda_device):
     pair = worker.evaluate_confirmation(dict(spec, order=order))
     assert pair["candidate"]["implementation"] == worker.CANDIDATE
     assert pair["torch"]["implementation"] == worker.BASELINES[kernel]
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+@pytest.mark.parametrize("shape", [(128, 256, 64), (256, 256, 64), (300, 520, 1000),
+                                   (257, 264, 4104), (1, 8, 8), (1000, 136, 200)])
+def test_cta_pair_gemm_edges(shape, dtype, cuda_device):
+    """tcgen05 cta_group::2 (CTA pairs, 256-row tiles): ragged M/N/K tails,
+    rows owned only by the second CTA of a pair, every stage depth."""
+    m, n, k = shape
+    g = torch.Generator().manual_seed(m * 13 + n)
+    a = torch.randn(m, k, generator=g).to(worker_dtype(dtype))
+    b = torch.randn(k, n, generator=g).to(worker_dtype(dtype))
+    ref = numerics.gemm_fp32(as_f32(a), as_f32(b))
+    a, b = a.to(cuda_device), b.to(cuda_device)
+    for bn, stages in ((256, 6), (256, 3), (128, 8), (128, 4)):
+        for group_m in (1, 8):
+            out = nan_like((m, n), dtype, cuda_device)
+            gemm.launch(a, b, out, {"BLOCK_N": bn, "num_stages": stages, "GROUP_M": group_m,
+                                    "CTA_GROUP": 2})
+            torch.cuda.synchronize()
+            gate(out, ref, dtype)
+
+
+def test_cta_pair_gemm_2048(cuda_device):
+    from flashattentionanycard_b200 import workloads
+
+    a, b = workloads.gemm_inputs(2048, 2048, 2048, "bf16", seed=1)
+    ref = numerics.gemm_fp32(as_f32(a), as_f32(b))
+    out = nan_like((2048, 2048), "bf16", cuda_device)
+    gemm.launch(a.to(cuda_device), b.to(cuda_device), out, {"CTA_GROUP": 2})
+    torch.cuda.synchronize()
+    gate(out, ref, "bf16")
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+@pytest.mark.parametrize("shape", [(1, 8), (3, 4096), (148, 1024), (1000, 4096), (4096, 4096),
+                                   (10, 14336), (5000, 520)])
+def test_rmsnorm_ring_kernel(shape, dtype, cuda_device):
+    """Persistent TMA-staged RMSNorm (num_stages >= 2): fewer rows than CTAs,
+    rows per CTA not a multiple of the consumer warps, wide rows."""
+    m, n = shape
+    g = torch.Generator().manual_seed(m + n)
+    x = torch.randn(m, n, generator=g).to(worker_dtype(dtype))
+    w = (1 + 0.1 * torch.randn(n, generator=g)).to(worker_dtype(dtype))
+    ref = numerics.rmsnorm_fp32(as_f32(x), as_f32(w), 1e-6)
+    xd, wd = x.to(cuda_device), w.to(cuda_device)
+    for warps, stages in ((8, 16), (4, 8), (1, 4), (16, 16), (2, 2)):
+        p = {"ROWS_PER_CTA": 1, "num_warps": warps, "num_stages": stages}
+        if n * 2 * (stages + 1) > 200 * 1024:
+            continue
+        out = nan_like((m, n), dtype, cuda_device)
+        compiled = rmsnorm.launch(xd, wd, out, p, 1e-6)
+        assert compiled.path == "ring"
+        torch.cuda.synchronize()
+        gate(out, ref, dtype)

@@ -12,6 +12,7 @@ from flashattentionanycard_b200.configs.search_spaces import (
 )
 from flashattentionanycard_b200.tuner.hardware import (
     Hardware,
+    gemm_pair_shared_bytes,
     gemm_shared_bytes,
     nvlink_topology,
     parse_topology,
@@ -50,7 +51,12 @@ def test_every_full_space_config_is_classified(hardware):
         legal = [p for p in grid_configs(search_space(kernel)) if prune_reason(hardware, kernel, p) is None]
         assert legal, kernel
         for p in legal:
-            assert gemm_shared_bytes(p["BLOCK_N"], p["num_stages"], 64) <= 227 * 1024
+            if p.get("CTA_GROUP", 1) == 2:
+                assert gemm_pair_shared_bytes(p["BLOCK_N"], p["num_stages"]) <= 227 * 1024
+            else:
+                assert gemm_shared_bytes(p["BLOCK_N"], p["num_stages"], 64) <= 227 * 1024
+        if kernel == "gemm":
+            assert any(p["CTA_GROUP"] == 2 for p in legal)
 
 
 def test_rmsnorm_limit(hardware):
