@@ -55,12 +55,61 @@ struct GemmTcShape {
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN must be 64, 128 or 256");
 };
 
+// Epilogue staging: per epilogue warp, 32 rows x 64 columns of 16-bit output
+// (4 KB) plus the 32 destination row pointers.
+constexpr int kEpiWarps = 4;
+constexpr int kEpiStageBytes = 32 * 128;
+constexpr int kEpiBytes = kEpiWarps * (kEpiStageBytes + 32 * 8);
+
 // Dynamic shared memory the kernel needs (host and device agree on this).
 __host__ __device__ inline int gemm_tc_smem_bytes(int bn, int stages, bool grouped, int experts) {
   int bytes = 1024 /* alignment slack */ + stages * (kGemmABytes + bn * kGemmBK * 2) +
-              (2 * stages + 4) * 8 + 16;
+              kEpiBytes + (2 * stages + 4) * 8 + 16;
   if (grouped) bytes += (3 * experts + 1) * 4;
   return bytes;
+}
+
+// One epilogue warp writes its 32 accumulator rows (TMEM lanes of this warp,
+// columns [0, BN) of the accumulator at `taddr`) to rows rowptr[0..31] (null:
+// row outside the problem), columns [n0, min(n0 + BN, N)).  Each 64-column
+// chunk goes TMEM -> registers -> round -> XOR-swizzled staging buffer, then
+// is written back with every group of 8 lanes storing one full 128-byte row
+// segment: coalesced HBM writes, and full-line NVLink writes when a row
+// pointer is a peer GPU's memory.
+template <int BN, typename OutT>
+__device__ __forceinline__ void epilogue_store_tile(uint32_t taddr, uint8_t* stage,
+                                                    OutT* const* rowptr, int n0, int N,
+                                                    int lane) {
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 64) {
+    uint32_t v0[32], v1[32];
+    tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c), v0);
+    tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c + 32), v1);
+    tmem_ld_wait();
+    uint8_t* my_row = stage + lane * 128;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t* v = j < 4 ? v0 : v1;
+      const int b = (j & 3) * 8;
+      uint4 pk;
+      pk.x = Pack2<OutT>::pack(__uint_as_float(v[b + 0]), __uint_as_float(v[b + 1]));
+      pk.y = Pack2<OutT>::pack(__uint_as_float(v[b + 2]), __uint_as_float(v[b + 3]));
+      pk.z = Pack2<OutT>::pack(__uint_as_float(v[b + 4]), __uint_as_float(v[b + 5]));
+      pk.w = Pack2<OutT>::pack(__uint_as_float(v[b + 6]), __uint_as_float(v[b + 7]));
+      *reinterpret_cast<uint4*>(my_row + ((j ^ (lane & 7)) << 4)) = pk;
+    }
+    __syncwarp();
+    const int cc = lane & 7;
+    const int col = n0 + c + cc * 8;
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int r = it * 4 + (lane >> 3);
+      const uint4 d = *reinterpret_cast<const uint4*>(stage + r * 128 + ((cc ^ (r & 7)) << 4));
+      OutT* rp = rowptr[r];
+      if (rp != nullptr && col < N) *reinterpret_cast<uint4*>(rp + c + cc * 8) = d;
+    }
+    __syncwarp();
+  }
 }
 
 struct TileCoord {
@@ -129,7 +178,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int stages = args.stages;
   uint8_t* sA = smem;
   uint8_t* sB = smem + stages * kGemmABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + stages * Shape::kBBytes);
+  uint8_t* sEpi = sB + stages * Shape::kBBytes;  // kEpiWarps x (staging + row pointers)
+  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + kEpiBytes);
   uint64_t* empty = full + stages;
   uint64_t* tfull = empty + stages;
   uint64_t* tempty = tfull + 2;
@@ -290,6 +340,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int r = q * 32 + lane;
     OutT* C = reinterpret_cast<OutT*>(args.C);
+    uint8_t* stage = sEpi + (warp - 2) * kEpiStageBytes;
+    OutT** rowptr = reinterpret_cast<OutT**>(sEpi + kEpiWarps * kEpiStageBytes) + (warp - 2) * 32;
     int i = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
       const TileCoord tc = tile_at(t);
@@ -315,25 +367,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       }
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c), v);
-        tmem_ld_wait();
-        if (row_ok) {
-#pragma unroll
-          for (int j = 0; j < 32; j += 8) {
-            if (tc.n0 + c + j < N) {  // N % 8 == 0 on this path: 8-column chunks are all-or-none
-              uint4 pk;
-              pk.x = Pack2<OutT>::pack(__uint_as_float(v[j + 0]), __uint_as_float(v[j + 1]));
-              pk.y = Pack2<OutT>::pack(__uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
-              pk.z = Pack2<OutT>::pack(__uint_as_float(v[j + 4]), __uint_as_float(v[j + 5]));
-              pk.w = Pack2<OutT>::pack(__uint_as_float(v[j + 6]), __uint_as_float(v[j + 7]));
-              *reinterpret_cast<uint4*>(crow + c + j) = pk;
-            }
-          }
-        }
-      }
+      rowptr[lane] = row_ok ? crow : nullptr;
+      __syncwarp();
+      epilogue_store_tile<BN, OutT>(taddr, stage, rowptr, tc.n0, N, lane);
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
     }

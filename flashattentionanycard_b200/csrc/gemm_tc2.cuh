@@ -31,7 +31,8 @@ struct GemmTc2Shape {
 };
 
 __host__ __device__ inline int gemm_tc2_smem_bytes(int bn, int stages) {
-  return 1024 + stages * (kGemmABytes + (bn / 2) * kGemmBK * 2) + (2 * stages + 4) * 8 + 16;
+  return 1024 + stages * (kGemmABytes + (bn / 2) * kGemmBK * 2) + kEpiBytes +
+         (2 * stages + 4) * 8 + 16;
 }
 
 template <int BN, typename OutT>
@@ -46,7 +47,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int stages = args.stages;
   uint8_t* sA = smem;
   uint8_t* sB = smem + stages * kGemmABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + stages * Shape::kBBytes);
+  uint8_t* sEpi = sB + stages * Shape::kBBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sEpi + kEpiBytes);
   uint64_t* empty = full + stages;
   uint64_t* tfull = empty + stages;
   uint64_t* tempty = tfull + 2;
@@ -175,6 +177,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int q = warp & 3;
     const int r = q * 32 + lane;
     OutT* C = reinterpret_cast<OutT*>(args.C);
+    uint8_t* stage = sEpi + (warp - 2) * kEpiStageBytes;
+    OutT** rowptr = reinterpret_cast<OutT**>(sEpi + kEpiWarps * kEpiStageBytes) + (warp - 2) * 32;
     int i = 0;
     for (int t = pair; t < ntiles; t += npairs, ++i) {
       int m0, n0;
@@ -187,27 +191,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const int row = m0 + static_cast<int>(rank) * kGemmBM + r;
-      const bool row_ok = row < M;
-      OutT* crow = C + static_cast<size_t>(row_ok ? row : 0) * N + n0;
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c), v);
-        tmem_ld_wait();
-        if (row_ok) {
-#pragma unroll
-          for (int j = 0; j < 32; j += 8) {
-            if (n0 + c + j < N) {
-              uint4 pk;
-              pk.x = Pack2<OutT>::pack(__uint_as_float(v[j + 0]), __uint_as_float(v[j + 1]));
-              pk.y = Pack2<OutT>::pack(__uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
-              pk.z = Pack2<OutT>::pack(__uint_as_float(v[j + 4]), __uint_as_float(v[j + 5]));
-              pk.w = Pack2<OutT>::pack(__uint_as_float(v[j + 6]), __uint_as_float(v[j + 7]));
-              *reinterpret_cast<uint4*>(crow + c + j) = pk;
-            }
-          }
-        }
-      }
+      rowptr[lane] = row < M ? C + static_cast<size_t>(row) * N + n0 : nullptr;
+      __syncwarp();
+      epilogue_store_tile<BN, OutT>(taddr, stage, rowptr, n0, N, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(map_shared(smem_addr(&tempty[acc]), 0));

@@ -19,6 +19,7 @@ from dataclasses import asdict, dataclass, field
 GEMM_BM, GEMM_BK = 128, 64
 GEMM_WARPS = 6
 TMEM_COLUMNS = 512
+EPILOGUE_BYTES = 4 * (32 * 128 + 32 * 8)  # staging + row pointers of the 4 epilogue warps
 
 
 @dataclass(frozen=True)
@@ -111,7 +112,7 @@ def gemm_shared_bytes(block_n, stages, experts=0):
     """Dynamic shared memory of the tcgen05 GEMM (csrc/gemm_tc.cuh gemm_tc_smem_bytes)."""
     a_bytes = GEMM_BM * GEMM_BK * 2
     b_bytes = block_n * GEMM_BK * 2
-    total = 1024 + stages * (a_bytes + b_bytes) + (2 * stages + 4) * 8 + 16
+    total = 1024 + stages * (a_bytes + b_bytes) + EPILOGUE_BYTES + (2 * stages + 4) * 8 + 16
     if experts:
         total += (3 * experts + 1) * 4
     return total
@@ -119,7 +120,8 @@ def gemm_shared_bytes(block_n, stages, experts=0):
 
 def gemm_pair_shared_bytes(block_n, stages):
     """Dynamic shared memory per CTA of the CTA-pair GEMM (csrc/gemm_tc2.cuh)."""
-    return 1024 + stages * (GEMM_BM * GEMM_BK * 2 + (block_n // 2) * GEMM_BK * 2) + (2 * stages + 4) * 8 + 16
+    return (1024 + stages * (GEMM_BM * GEMM_BK * 2 + (block_n // 2) * GEMM_BK * 2)
+            + EPILOGUE_BYTES + (2 * stages + 4) * 8 + 16)
 
 
 def rmsnorm_ring_bytes(columns, stages, elem_bytes=2):
