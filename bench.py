@@ -42,6 +42,7 @@ METRIC = "TFLOP/s (GEMM, MoE grouped GEMM) & RMSNorm GB/s vs B200 peak at 1–8 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 L2_BYTES = 126 * 1024 * 1024
 EP_COMM = "peer"  # --ep-comm: expert-parallel dispatch/combine over NVLink peer stores or NCCL
+MOE_EXPERTS = None  # --experts: moe_large with fewer experts (small profiling case)
 # Rotating input sets together span 4x L2, so a set is long evicted when it is reused.
 ROTATION_BYTES = 4 * L2_BYTES
 
@@ -431,11 +432,13 @@ class MoeLarge:
         from flashattentionanycard_b200.configs.search_spaces import default_params
         from flashattentionanycard_b200.kernels.moe_routing import MoeRouter
 
-        cfg = workloads.MOE_LARGE
+        cfg = dict(workloads.MOE_LARGE)
+        cfg["experts"] = MOE_EXPERTS or cfg["experts"]
         self.cfg = cfg
         self.world, self.rank = world, rank
         self.params = default_params("moe_grouped_gemm")
-        self.x, self.w, ids = workloads.moe_large_inputs("bf16", seed=0, device=device)
+        self.x, self.w, ids = workloads.moe_large_inputs("bf16", seed=0, device=device,
+                                                         experts=cfg["experts"])
         self.sm = torch.cuda.get_device_properties(device).multi_processor_count
         a = ids.numel()
         self.flops_per_step = 2.0 * a * cfg["k"] * cfg["n"]  # whole job, all ranks
@@ -906,11 +909,15 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="rmsnorm")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--experts", type=int, default=None,
+                    help="moe_large with this many experts instead of 64 (a smaller case of the "
+                         "same kernel, e.g. for ncu captures)")
     ap.add_argument("--ep-comm", choices=("peer", "nccl"), default="peer",
                     help="moe_large at N>1: NVLink peer stores (fused) or NCCL all-to-all")
     args = ap.parse_args()
-    global EP_COMM
+    global EP_COMM, MOE_EXPERTS
     EP_COMM = args.ep_comm
+    MOE_EXPERTS = args.experts
     if args.steps is None:
         args.steps = 20 if args.impl == "reference" else DEFAULT_STEPS[args.workload]
     if args.warmup < 3:
