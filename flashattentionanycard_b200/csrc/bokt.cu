@@ -807,6 +807,59 @@ int bokt_ipc_close(void* base) {
   return BOKT_OK;
 }
 
+int bokt_moe_topk_gate(const void* logits, int logits_dtype, int tokens, int E, int k,
+                       int renormalize, int32_t* ids, float* gates, void* stream) {
+  g_err[0] = 0;
+  if (tokens < 0 || E <= 0 || k <= 0) return fail(BOKT_ERR_INVALID, "bad size");
+  if (k > bokt::kTopkMax || k > E)
+    return fail(BOKT_ERR_UNSUPPORTED, "k must be <= %d and <= E", bokt::kTopkMax);
+  if (E > bokt::kGateMaxExperts)
+    return fail(BOKT_ERR_UNSUPPORTED, "at most %d experts", bokt::kGateMaxExperts);
+  if (tokens == 0) return BOKT_OK;
+  if (!logits || !ids || !gates) return fail(BOKT_ERR_INVALID, "null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int grid = (tokens + 7) / 8;
+  if (grid > 148 * 32) grid = 148 * 32;
+  cudaError_t e;
+  if (logits_dtype == BOKT_BF16)
+    e = launch(bokt::moe_topk_gate_kernel<__nv_bfloat16>, dim3(grid), dim3(256), 0, s,
+               static_cast<const __nv_bfloat16*>(logits), tokens, E, k, renormalize, ids, gates);
+  else if (logits_dtype == BOKT_FP16)
+    e = launch(bokt::moe_topk_gate_kernel<__half>, dim3(grid), dim3(256), 0, s,
+               static_cast<const __half*>(logits), tokens, E, k, renormalize, ids, gates);
+  else if (logits_dtype == BOKT_FP32)
+    e = launch(bokt::moe_topk_gate_kernel<float>, dim3(grid), dim3(256), 0, s,
+               static_cast<const float*>(logits), tokens, E, k, renormalize, ids, gates);
+  else
+    return fail(BOKT_ERR_INVALID, "logits dtype %d", logits_dtype);
+  if (e != cudaSuccess) return cuda_fail(e, "moe_topk_gate launch");
+  return BOKT_OK;
+}
+
+int bokt_moe_combine(const void* y, int64_t y_rows, const int32_t* rows, const float* gates,
+                     void* out, int tokens, int k, int N, int dtype, void* stream) {
+  g_err[0] = 0;
+  if (dtype != BOKT_FP16 && dtype != BOKT_BF16) return fail(BOKT_ERR_INVALID, "dtype %d", dtype);
+  if (tokens < 0 || k <= 0 || N < 0 || y_rows < 0) return fail(BOKT_ERR_INVALID, "bad size");
+  if (tokens == 0 || N == 0) return BOKT_OK;
+  if (!y || !gates || !out) return fail(BOKT_ERR_INVALID, "null pointer");
+  if (N % 8 != 0 || !aligned16(y) || !aligned16(out))
+    return fail(BOKT_ERR_UNSUPPORTED, "combine needs N %% 8 == 0 and 16-byte aligned rows");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int grid = tokens < 148 * 64 ? tokens : 148 * 64;
+  const int threads = N / 8 < 256 ? ((N / 8 + 31) / 32) * 32 : 256;
+  cudaError_t e =
+      dtype == BOKT_BF16
+          ? launch(bokt::moe_combine_kernel<__nv_bfloat16>, dim3(grid), dim3(threads), 0, s,
+                   static_cast<const __nv_bfloat16*>(y), (long long)y_rows, rows, gates,
+                   static_cast<__nv_bfloat16*>(out), tokens, k, N)
+          : launch(bokt::moe_combine_kernel<__half>, dim3(grid), dim3(threads), 0, s,
+                   static_cast<const __half*>(y), (long long)y_rows, rows, gates,
+                   static_cast<__half*>(out), tokens, k, N);
+  if (e != cudaSuccess) return cuda_fail(e, "moe_combine launch");
+  return BOKT_OK;
+}
+
 int bokt_kernel_attrs(int kernel, int dtype, int n, int k, const bokt_params* params,
                       bokt_attrs* out) {
   g_err[0] = 0;

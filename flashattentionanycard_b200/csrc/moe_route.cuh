@@ -398,3 +398,128 @@ __global__ void ep_rowmap_kernel(const int32_t* __restrict__ perm,
 }
 
 }  // namespace bokt
+
+namespace bokt {
+
+constexpr int kTopkMax = 8;
+constexpr int kGateMaxExperts = 1024;
+
+template <typename T>
+__device__ __forceinline__ float load_logit(const T* p) {
+  return Pack2<T>::to_float(*p);
+}
+template <>
+__device__ __forceinline__ float load_logit<float>(const float* p) {
+  return *p;
+}
+
+// Top-k softmax gate: one warp per token.  p = softmax(logits[t, :]) in fp32;
+// ids[t, j] = index of the j-th largest p (ties: lower expert index first);
+// gates[t, j] = p[ids[t, j]], divided by their sum when `renormalize`.
+template <typename T>
+__global__ void __launch_bounds__(256) moe_topk_gate_kernel(const T* __restrict__ logits, int tokens,
+                                                            int E, int k, int renormalize,
+                                                            int32_t* __restrict__ ids,
+                                                            float* __restrict__ gates) {
+  pdl_allow_next();
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  for (int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < tokens; t += warps) {
+    const T* row = logits + static_cast<long long>(t) * E;
+    float mx = -INFINITY;
+    for (int e = lane; e < E; e += 32) mx = fmaxf(mx, load_logit(row + e));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.f;
+    for (int e = lane; e < E; e += 32) sum += expf(load_logit(row + e) - mx);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    // k rounds of a warp-wide arg-max over the logits not yet taken.
+    int taken[kTopkMax];
+    float picked = 0.f;
+    float vals[kTopkMax];
+    for (int j = 0; j < k; ++j) {
+      float best = -INFINITY;
+      int best_e = E;
+      for (int e = lane; e < E; e += 32) {
+        bool used = false;
+        for (int i = 0; i < j; ++i) used |= (taken[i] == e);
+        const float v = load_logit(row + e);
+        if (!used && (v > best || (v == best && e < best_e))) {
+          best = v;
+          best_e = e;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oe = __shfl_xor_sync(0xffffffffu, best_e, o);
+        if (ov > best || (ov == best && oe < best_e)) {
+          best = ov;
+          best_e = oe;
+        }
+      }
+      taken[j] = best_e;
+      vals[j] = expf(best - mx) / sum;
+      picked += vals[j];
+    }
+    if (lane == 0) {
+      for (int j = 0; j < k; ++j) {
+        ids[static_cast<long long>(t) * k + j] = taken[j];
+        gates[static_cast<long long>(t) * k + j] = renormalize ? vals[j] / picked : vals[j];
+      }
+    }
+  }
+}
+
+// Gate-weighted combine back to token order:
+//   out[t, :] = sum_j gates[t, j] * y[row(t, j), :],  row = rows ? rows[t*k + j] : t*k + j
+// fp32 accumulation, rounded on store; one CTA slice per token, 16-byte vectors.
+template <typename T>
+__global__ void __launch_bounds__(256) moe_combine_kernel(const T* __restrict__ y, long long y_rows,
+                                                          const int32_t* __restrict__ rows,
+                                                          const float* __restrict__ gates,
+                                                          T* __restrict__ out, int tokens, int k,
+                                                          int N) {
+  pdl_allow_next();
+  pdl_wait();
+  const int nvec = N / 8;
+  const uint4* yv4 = reinterpret_cast<const uint4*>(y);
+  bool bad = false;
+  for (int t = blockIdx.x; t < tokens; t += gridDim.x) {
+    for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+      for (int j = 0; j < k; ++j) {
+        const int a = t * k + j;
+        const long long r = rows ? static_cast<long long>(rows[a]) : static_cast<long long>(a);
+        if (r < 0 || r >= y_rows) {
+          bad = true;
+          continue;
+        }
+        const float g = gates[a];
+        const uint4 yv = yv4[r * nvec + v];
+        const float2 f0 = Pack2<T>::unpack(yv.x), f1 = Pack2<T>::unpack(yv.y);
+        const float2 f2 = Pack2<T>::unpack(yv.z), f3 = Pack2<T>::unpack(yv.w);
+        acc[0] = fmaf(g, f0.x, acc[0]);
+        acc[1] = fmaf(g, f0.y, acc[1]);
+        acc[2] = fmaf(g, f1.x, acc[2]);
+        acc[3] = fmaf(g, f1.y, acc[3]);
+        acc[4] = fmaf(g, f2.x, acc[4]);
+        acc[5] = fmaf(g, f2.y, acc[5]);
+        acc[6] = fmaf(g, f3.x, acc[6]);
+        acc[7] = fmaf(g, f3.y, acc[7]);
+      }
+      uint4 o;
+      o.x = Pack2<T>::pack(acc[0], acc[1]);
+      o.y = Pack2<T>::pack(acc[2], acc[3]);
+      o.z = Pack2<T>::pack(acc[4], acc[5]);
+      o.w = Pack2<T>::pack(acc[6], acc[7]);
+      reinterpret_cast<uint4*>(out + static_cast<long long>(t) * N)[v] = o;
+    }
+  }
+  if (bad) report_status(kStatusBadExpertId, blockIdx.x);
+}
+
+}  // namespace bokt

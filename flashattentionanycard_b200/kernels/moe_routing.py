@@ -96,3 +96,41 @@ class MoeRouter:
         route(expert_ids.reshape(-1), self.experts, self.counts, self.offsets, self.perm,
               self.inv_perm, self.workspace, self.offsets64)
         return self
+
+
+def topk_gate(logits, k, ids, gates, renormalize=True):
+    """Top-k softmax gate on the device: ids [T, k] int32, gates [T, k] fp32
+    (softmax of the logits at the picked experts, renormalised to sum 1 when
+    ``renormalize``); ties go to the lower expert index."""
+    import torch
+
+    t, e = logits.shape
+    codes = {torch.float16: _native.FP16, torch.bfloat16: _native.BF16, torch.float32: 2}
+    if logits.dtype not in codes or not logits.is_contiguous():
+        raise ValueError("logits must be a contiguous fp16/bf16/fp32 [tokens, experts] tensor")
+    if ids.dtype != torch.int32 or tuple(ids.shape) != (t, k) or not ids.is_contiguous():
+        raise ValueError("ids must be a contiguous int32 [tokens, k] tensor")
+    if gates.dtype != torch.float32 or tuple(gates.shape) != (t, k) or not gates.is_contiguous():
+        raise ValueError("gates must be a contiguous fp32 [tokens, k] tensor")
+    _native.check(_native.load().bokt_moe_topk_gate(
+        logits.data_ptr(), codes[logits.dtype], t, e, int(k), 1 if renormalize else 0,
+        ids.data_ptr(), gates.data_ptr(), _native.current_stream(logits.device)),
+        "bokt_moe_topk_gate")
+
+
+def combine(y, gates, out, rows=None):
+    """out[t] = sum_j gates[t, j] * y[rows[t*k + j] if rows is given else t*k + j]
+    on the device (fp32 accumulation)."""
+    import torch
+
+    t, k = gates.shape
+    if gates.dtype != torch.float32 or not gates.is_contiguous():
+        raise ValueError("gates must be a contiguous fp32 [tokens, k] tensor")
+    if y.dtype != out.dtype or y.shape[1] != out.shape[1] or out.shape[0] != t:
+        raise ValueError("y [rows, N] and out [tokens, N] must share dtype and N")
+    if rows is not None and (rows.dtype != torch.int32 or rows.numel() != t * k):
+        raise ValueError("rows must be int32 with tokens * k entries")
+    _native.check(_native.load().bokt_moe_combine(
+        y.data_ptr(), y.shape[0], rows.data_ptr() if rows is not None else None, gates.data_ptr(),
+        out.data_ptr(), t, int(k), y.shape[1], _native.dtype_code(y.dtype),
+        _native.current_stream(y.device)), "bokt_moe_combine")

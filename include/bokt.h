@@ -40,6 +40,7 @@ extern "C" {
 /* element types (values match the tcgen05 kind::f16 operand format codes) */
 #define BOKT_FP16 0
 #define BOKT_BF16 1
+#define BOKT_FP32 2 /* router logits only */
 
 /* status codes */
 #define BOKT_OK 0
@@ -280,6 +281,27 @@ int bokt_ep_rowmap(const int32_t* perm, const int32_t* ids, const int32_t* offse
 int bokt_ipc_export(const void* ptr, void* handle_out, int64_t* offset_out);
 int bokt_ipc_import(const void* handle, int64_t offset, void** base_out, void** ptr_out);
 int bokt_ipc_close(void* base);
+
+/*
+ * Top-k softmax gate (routing front end): per token t, p = softmax(logits[t, :])
+ * in fp32; ids[t, j] (int32 [tokens, k]) = the j-th largest p, ties to the
+ * lower expert index; gates[t, j] (fp32) = p of that expert, divided by the sum
+ * of the k picked when renormalize != 0.  logits: [tokens, E] fp16/bf16/fp32.
+ * k <= 8, E <= 1024.  No counterpart in the reference (routing is outside
+ * kernels/moe_grouped_gemm.py:3).
+ */
+int bokt_moe_topk_gate(const void* logits, int logits_dtype, int tokens, int E, int k,
+                       int renormalize, int32_t* ids, float* gates, void* stream);
+
+/*
+ * Gate-weighted combine: out[t, :] = sum_j gates[t, j] * y[row, :] with
+ * row = rows[t * k + j] (e.g. the routing's inv_perm when y is packed by
+ * expert) or t * k + j when rows is NULL (y in assignment order); fp32
+ * accumulation, rounded to dtype.  N % 8 == 0.  A row outside y sets the
+ * device status word.  No counterpart in the reference.
+ */
+int bokt_moe_combine(const void* y, int64_t y_rows, const int32_t* rows, const float* gates,
+                     void* out, int tokens, int k, int N, int dtype, void* stream);
 
 /* Resource usage of the kernel a call with these arguments would launch. */
 int bokt_kernel_attrs(int kernel, int dtype, int n, int k, const bokt_params* params,

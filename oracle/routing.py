@@ -54,3 +54,29 @@ def route(ids, experts):
     perm = stable_permutation(ids, experts)
     return counts, expert_offsets(counts), perm, inverse_permutation(perm)
 
+
+
+def topk_gate(logits, k, renormalize=True):
+    """(ids int32 [T, k], gates float32 [T, k]): the k largest logits per row
+    (ties: lower expert index first) and their softmax probabilities, computed
+    in float64 and optionally renormalised over the picked experts."""
+    logits = np.asarray(logits, dtype=np.float64)
+    t, e = logits.shape
+    order = np.lexsort((np.broadcast_to(np.arange(e), (t, e)), -logits), axis=-1)
+    ids = order[:, :k]
+    z = logits - logits.max(axis=1, keepdims=True)
+    p = np.exp(z) / np.exp(z).sum(axis=1, keepdims=True)
+    gates = np.take_along_axis(p, ids, axis=1)
+    if renormalize:
+        gates = gates / gates.sum(axis=1, keepdims=True)
+    return ids.astype(np.int32), gates.astype(np.float32)
+
+
+def combine(y, gates, rows=None):
+    """out[t] = sum_j gates[t, j] * y[row(t, j)] in float32."""
+    y = np.asarray(y, dtype=np.float32)
+    gates = np.asarray(gates, dtype=np.float32)
+    t, k = gates.shape
+    idx = np.arange(t * k) if rows is None else np.asarray(rows, dtype=np.int64)
+    picked = y[idx].reshape(t, k, -1)
+    return np.einsum("tk,tkn->tn", gates, picked).astype(np.float32)

@@ -106,3 +106,26 @@ def test_grouped_oracle_leaves_uncovered_rows():
     out = numerics.grouped_gemm_fp32(x, w, [1, 3, 5])
     assert np.isnan(out[0]).all() and np.isnan(out[5]).all()
     assert np.all(out[1:5] == 2.0)
+
+
+def test_topk_gate_oracle_against_sorting():
+    rng = np.random.default_rng(0)
+    logits = rng.standard_normal((50, 64)).astype(np.float32)
+    logits[3, [5, 9]] = 7.0  # a tie: the lower index comes first
+    ids, gates = routing.topk_gate(logits, 2)
+    for t in range(50):
+        want = sorted(range(64), key=lambda e: (-float(logits[t, e]), e))[:2]
+        assert ids[t].tolist() == want
+    assert ids[3].tolist() == [5, 9]
+    np.testing.assert_allclose(gates.sum(axis=1), 1.0, rtol=1e-6)
+    raw_ids, raw = routing.topk_gate(logits, 2, renormalize=False)
+    assert np.array_equal(raw_ids, ids) and np.all(raw.sum(axis=1) < 1.0)
+
+
+def test_combine_oracle():
+    y = np.arange(12, dtype=np.float32).reshape(6, 2)
+    gates = np.array([[0.5, 0.5], [1.0, 0.0], [0.25, 0.75]], np.float32)
+    out = routing.combine(y, gates)
+    assert np.allclose(out, [[1, 2], [4, 5], [0.25 * 8 + 0.75 * 10, 0.25 * 9 + 0.75 * 11]])
+    perm_rows = np.array([5, 4, 3, 2, 1, 0])
+    assert np.allclose(routing.combine(y, gates, perm_rows)[0], 0.5 * y[5] + 0.5 * y[4])
