@@ -197,7 +197,8 @@ class CompiledKernel:
         self.n_regs = int(attrs.registers)
         self.n_spills = int(attrs.local_bytes) // 4
         self.threads = int(attrs.threads)
-        self.path = {0: "tcgen05", 1: "simt", 2: "vector", 3: "scalar", 4: "ring"}.get(attrs.path, "?")
+        self.path = {0: "tcgen05", 1: "simt", 2: "vector", 3: "scalar", 4: "ring",
+                     5: "pipelined"}.get(attrs.path, "?")
 
 
 _attr_cache = {}

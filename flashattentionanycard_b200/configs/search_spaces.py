@@ -15,10 +15,12 @@ kernels:
 * GEMM only: ``CTA_GROUP`` 1 (one CTA per 128-row tile) or 2 (CTA pairs on two
   SMs, tcgen05 cta_group::2, 256-row tiles).
 * RMSNorm: ``ROWS_PER_CTA`` and ``num_warps`` as in the reference, plus
-  ``num_stages``: 1 keeps the reference's one-row-slice-per-CTA shape;
-  2 or more selects the persistent kernel in which a producer warp streams
-  rows into a ring of that many shared-memory row buffers (cp.async.bulk) and
-  ``num_warps`` consumer warps normalise one row each.
+  ``num_stages``: 1 keeps the reference's one-row-slice-per-CTA shape; 2 (with
+  ROWS_PER_CTA 1) a persistent CTA per resident slot that keeps its next row's
+  loads in flight in a second register buffer; 4 or more the persistent kernel
+  in which a producer warp streams rows into a ring of that many shared-memory
+  row buffers (cp.async.bulk) and ``num_warps`` consumer warps normalise one
+  row each.
 """
 
 from dataclasses import asdict, dataclass
@@ -73,7 +75,7 @@ def search_space(kernel: str, profile: str = "full") -> dict[str, list[int]]:
         return {
             "ROWS_PER_CTA": [1, 2, 4, 8] if profile == "full" else [1, 2],
             "num_warps": [1, 2, 4, 8, 16] if profile == "full" else [4, 8],
-            "num_stages": [1, 4, 8, 16] if profile == "full" else [1, 8],
+            "num_stages": [1, 2, 4, 8, 16] if profile == "full" else [1, 2, 8],
         }
     space = {
         "BLOCK_M": [128],

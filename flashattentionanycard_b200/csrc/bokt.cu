@@ -333,7 +333,13 @@ int resolve_norm_config(const bokt_params* p, int N, bool vec_ok, NormConfig* ou
   // 16-byte aligned); odd or unaligned rows take the per-row kernels instead,
   // as odd GEMM shapes take the SIMT edge path.
   int ring = 0;
-  if (stages >= 2 && vec_ok) {
+  if (stages == 2 && vec_ok && rows == 1 && vpt > 0 && vpt <= 8) {
+    // Two register buffers: the persistent software-pipelined kernel (one row
+    // per CTA at a time).  Other shapes keep the per-row kernels.
+    *out = {rows, threads, lg, vpt, -1};
+    return BOKT_OK;
+  }
+  if (stages >= 4 && vec_ok) {
     if (warps > 31) return fail(BOKT_ERR_CONFIG, "ring kernel: num_warps must be <= 31");
     if (stages % warps != 0)
       return fail(BOKT_ERR_CONFIG,
@@ -363,6 +369,17 @@ int launch_route(const int32_t* ids, int A, int E, int32_t* scratch, int32_t* co
                E, static_cast<const int32_t*>(scratch), perm, inv_perm);
   if (e != cudaSuccess) return cuda_fail(e, what);
   return BOKT_OK;
+}
+
+template <typename T>
+const void* pipe_kernel(int vpt) {
+  switch (vpt) {
+    case 1: return reinterpret_cast<const void*>(&bokt::rmsnorm_pipe_kernel<T, 1>);
+    case 2: return reinterpret_cast<const void*>(&bokt::rmsnorm_pipe_kernel<T, 2>);
+    case 4: return reinterpret_cast<const void*>(&bokt::rmsnorm_pipe_kernel<T, 4>);
+    case 8: return reinterpret_cast<const void*>(&bokt::rmsnorm_pipe_kernel<T, 8>);
+  }
+  return nullptr;
 }
 
 template <typename T>
@@ -615,6 +632,24 @@ int bokt_rmsnorm(const void* X, const void* W, void* Y, int M, int N, float eps,
   NormConfig cfg;
   int rc = resolve_norm_config(params, N, vec_ok, &cfg);
   if (rc) return rc;
+  if (cfg.ring_slots < 0) {
+    DeviceInfo dev;
+    rc = device_info(&dev);
+    if (rc) return rc;
+    const void* pfn = dtype == BOKT_BF16 ? pipe_kernel<__nv_bfloat16>(cfg.vpt)
+                                         : pipe_kernel<__half>(cfg.vpt);
+    int per_sm = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pfn, cfg.threads, 0);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    if (per_sm < 1) per_sm = 1;
+    long long grid = (long long)dev.sm_count * per_sm;
+    if (grid > M) grid = M;
+    void* pargs[] = {const_cast<void**>(&X), const_cast<void**>(&W), &Y, &M, &N, &eps,
+                     &cfg.tpr_log2};
+    e = launch_ptr(pfn, dim3(unsigned(grid)), dim3(cfg.threads), 0, s, pargs);
+    if (e != cudaSuccess) return cuda_fail(e, "rmsnorm pipe launch");
+    return BOKT_OK;
+  }
   if (cfg.ring_slots > 0) {
     DeviceInfo dev;
     rc = device_info(&dev);
@@ -890,7 +925,11 @@ int bokt_kernel_attrs(int kernel, int dtype, int n, int k, const bokt_params* pa
     NormConfig cfg;
     rc = resolve_norm_config(params, n, (n % 8) == 0, &cfg);
     if (rc) return rc;
-    if (cfg.ring_slots > 0) {
+    if (cfg.ring_slots < 0) {
+      fn = dtype == BOKT_BF16 ? pipe_kernel<__nv_bfloat16>(cfg.vpt) : pipe_kernel<__half>(cfg.vpt);
+      threads = cfg.threads;
+      path = 5;
+    } else if (cfg.ring_slots > 0) {
       fn = dtype == BOKT_BF16
                ? reinterpret_cast<const void*>(&bokt::rmsnorm_ring_kernel<__nv_bfloat16>)
                : reinterpret_cast<const void*>(&bokt::rmsnorm_ring_kernel<__half>);

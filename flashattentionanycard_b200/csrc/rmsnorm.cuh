@@ -245,3 +245,72 @@ __host__ __device__ inline int rmsnorm_ring_smem_bytes(int n, int elem_bytes, in
 }
 
 }  // namespace bokt
+
+namespace bokt {
+
+// Persistent RMSNorm with two register buffers per thread (N % 8 == 0, aligned):
+// grid = SMs x resident CTAs; CTA c handles rows c, c + grid, ...  The loads
+// of the CTA's next row are issued before the current row is reduced and
+// stored, so every SM keeps a row per CTA in flight continuously, and whole
+// SMs carry equal row counts (no partial last wave).
+template <typename T, int VPT>
+__global__ void rmsnorm_pipe_kernel(const T* __restrict__ X, const T* __restrict__ W,
+                                    T* __restrict__ Y, int M, int N, float eps, int tpr_log2) {
+  __shared__ float red[32];
+  pdl_allow_next();
+  pdl_wait();
+  const int tpr = 1 << tpr_log2;  // == blockDim.x: one row per CTA at a time
+  const int tid = threadIdx.x;
+  const int nvec = N >> 3;
+  uint4 wv[VPT];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int v = tid + j * tpr;
+    wv[j] = v < nvec ? __ldg(reinterpret_cast<const uint4*>(W) + v) : make_uint4(0, 0, 0, 0);
+  }
+  uint4 cur[VPT], nxt[VPT];
+  int row = blockIdx.x;
+  auto load_row = [&](int r, uint4 (&buf)[VPT]) {
+    const uint4* xr = reinterpret_cast<const uint4*>(X + static_cast<size_t>(r) * N);
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int v = tid + j * tpr;
+      buf[j] = (r < M && v < nvec) ? __ldg(xr + v) : make_uint4(0, 0, 0, 0);
+    }
+  };
+  load_row(row, cur);
+  for (; row < M; row += gridDim.x) {
+    load_row(row + gridDim.x, nxt);  // in flight while this row is reduced and stored
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const float2 a = Pack2<T>::unpack(cur[j].x), b = Pack2<T>::unpack(cur[j].y);
+      const float2 c = Pack2<T>::unpack(cur[j].z), d = Pack2<T>::unpack(cur[j].w);
+      ss = fmaf(a.x, a.x, ss); ss = fmaf(a.y, a.y, ss); ss = fmaf(b.x, b.x, ss); ss = fmaf(b.y, b.y, ss);
+      ss = fmaf(c.x, c.x, ss); ss = fmaf(c.y, c.y, ss); ss = fmaf(d.x, d.x, ss); ss = fmaf(d.y, d.y, ss);
+    }
+    ss = row_reduce_sum<T>(ss, tpr_log2, red);
+    const float scale = rsqrtf(ss / static_cast<float>(N) + eps);
+    uint4* yr = reinterpret_cast<uint4*>(Y + static_cast<size_t>(row) * N);
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int v = tid + j * tpr;
+      if (v < nvec) {
+        const float2 xa = Pack2<T>::unpack(cur[j].x), xb = Pack2<T>::unpack(cur[j].y);
+        const float2 xc = Pack2<T>::unpack(cur[j].z), xd = Pack2<T>::unpack(cur[j].w);
+        const float2 wa = Pack2<T>::unpack(wv[j].x), wb = Pack2<T>::unpack(wv[j].y);
+        const float2 wc = Pack2<T>::unpack(wv[j].z), wd = Pack2<T>::unpack(wv[j].w);
+        uint4 o;
+        o.x = Pack2<T>::pack((xa.x * scale) * wa.x, (xa.y * scale) * wa.y);
+        o.y = Pack2<T>::pack((xb.x * scale) * wb.x, (xb.y * scale) * wb.y);
+        o.z = Pack2<T>::pack((xc.x * scale) * wc.x, (xc.y * scale) * wc.y);
+        o.w = Pack2<T>::pack((xd.x * scale) * wd.x, (xd.y * scale) * wd.y);
+        yr[v] = o;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) cur[j] = nxt[j];
+  }
+}
+
+}  // namespace bokt

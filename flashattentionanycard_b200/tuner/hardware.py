@@ -141,7 +141,7 @@ def resource_estimate(kernel, params, columns=0, experts=0):
             "threads_per_row": per_row,
             "vectors_per_thread": vectors,
             "single_pass_registers": vectors <= 16 and columns % 8 == 0,
-            "shared_bytes_estimate": rmsnorm_ring_bytes(columns, stages) if stages >= 2 else 128,
+            "shared_bytes_estimate": rmsnorm_ring_bytes(columns, stages) if stages >= 4 else 128,
         }
     return {
         "shared_bytes_estimate": gemm_shared_bytes(params["BLOCK_N"], params["num_stages"], experts),
@@ -161,7 +161,7 @@ def prune_reason(hardware, kernel, params, columns=0, heuristic_smem=False):
         if params["ROWS_PER_CTA"] > warps * hardware.warp_size:
             return "rmsnorm_implementation_limit"
         stages = params.get("num_stages", 1)
-        if stages >= 2 and columns % 8 == 0:
+        if stages >= 4 and columns % 8 == 0:
             # Ring kernel: each ring slot must always be consumed by the same warp.
             if stages % warps or (warps + 1) * hardware.warp_size > hardware.max_threads_per_block:
                 return "rmsnorm_implementation_limit"

@@ -88,7 +88,7 @@ typedef struct bokt_attrs {
   int32_t local_bytes;    /* local memory per thread (spill indicator) */
   int32_t threads;        /* threads per CTA */
   int32_t max_threads;    /* cudaFuncAttributes.maxThreadsPerBlock */
-  int32_t path;           /* 0 = tcgen05/TMA, 1 = SIMT edge, 2 = vector, 3 = scalar, 4 = ring */
+  int32_t path; /* 0 tcgen05/TMA, 1 SIMT edge, 2 vector, 3 scalar, 4 ring, 5 pipelined */
 } bokt_attrs;
 
 /* ABI version and the sm architecture the library was built for (100). */

@@ -316,10 +316,33 @@ def test_rmsnorm_ring_kernel(shape, dtype, cuda_device):
     xd, wd = x.to(cuda_device), w.to(cuda_device)
     for warps, stages in ((8, 16), (4, 8), (1, 4), (16, 16), (2, 2)):
         p = {"ROWS_PER_CTA": 1, "num_warps": warps, "num_stages": stages}
-        if n * 2 * (stages + 1) > 200 * 1024:
+        if n * 2 * (stages + 1) > 200 * 1024 or stages < 4:
             continue
         out = nan_like((m, n), dtype, cuda_device)
         compiled = rmsnorm.launch(xd, wd, out, p, 1e-6)
         assert compiled.path == "ring"
+        torch.cuda.synchronize()
+        gate(out, ref, dtype)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+@pytest.mark.parametrize("shape", [(1, 8), (3, 4096), (148, 1024), (4096, 4096), (5000, 520),
+                                   (20000, 2048), (7, 8192)])
+def test_rmsnorm_pipelined_kernel(shape, dtype, cuda_device):
+    """Persistent software-pipelined RMSNorm (num_stages 2): fewer rows than
+    CTAs, several rows per CTA, next-row loads past the last row."""
+    m, n = shape
+    g = torch.Generator().manual_seed(3 * m + n)
+    x = torch.randn(m, n, generator=g).to(worker_dtype(dtype))
+    w = (1 + 0.1 * torch.randn(n, generator=g)).to(worker_dtype(dtype))
+    ref = numerics.rmsnorm_fp32(as_f32(x), as_f32(w), 1e-6)
+    xd, wd = x.to(cuda_device), w.to(cuda_device)
+    for warps in (1, 2, 4, 8):
+        out = nan_like((m, n), dtype, cuda_device)
+        compiled = rmsnorm.launch(xd, wd, out, {"ROWS_PER_CTA": 1, "num_warps": warps,
+                                               "num_stages": 2}, 1e-6)
+        per_thread = -(-(n // 8) // (warps * 32))
+        assert compiled.path == ("pipelined" if per_thread <= 8 else
+                                 "vector" if per_thread <= 16 else "scalar")
         torch.cuda.synchronize()
         gate(out, ref, dtype)
