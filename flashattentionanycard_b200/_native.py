@@ -97,6 +97,7 @@ SIGNATURES = {
     "bokt_ipc_export": (_I32, [_VP, _VP, ctypes.POINTER(ctypes.c_int64)]),
     "bokt_ipc_import": (_I32, [_VP, _I64, ctypes.POINTER(_VP), ctypes.POINTER(_VP)]),
     "bokt_ipc_close": (_I32, [_VP]),
+    "bokt_selftest_bounded_wait": (_I32, [_I64, _VP, _VP]),
     "bokt_moe_topk_gate": (_I32, [_VP, _I32, _I32, _I32, _I32, _I32, _VP, _VP, _VP]),
     "bokt_moe_combine": (_I32, [_VP, _I64, _VP, _VP, _VP, _I32, _I32, _I32, _I32, _VP]),
     "bokt_kernel_attrs": (

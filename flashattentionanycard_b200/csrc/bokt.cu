@@ -895,6 +895,16 @@ int bokt_moe_combine(const void* y, int64_t y_rows, const int32_t* rows, const f
   return BOKT_OK;
 }
 
+int bokt_selftest_bounded_wait(int64_t timeout_ns, int* gave_up, void* stream) {
+  g_err[0] = 0;
+  if (timeout_ns <= 0 || timeout_ns > 10000000000ll || !gave_up)
+    return fail(BOKT_ERR_INVALID, "timeout must be in (0, 10 s] and gave_up non-null");
+  cudaError_t e = launch(bokt::selftest_bounded_wait_kernel, dim3(1), dim3(32), 0,
+                         static_cast<cudaStream_t>(stream), uint64_t(timeout_ns), gave_up);
+  if (e != cudaSuccess) return cuda_fail(e, "selftest launch");
+  return BOKT_OK;
+}
+
 int bokt_kernel_attrs(int kernel, int dtype, int n, int k, const bokt_params* params,
                       bokt_attrs* out) {
   g_err[0] = 0;

@@ -90,9 +90,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 
 // Waits for the phase of `parity` to complete.  Returns false (after flagging
 // the CTA-wide abort word and the device status) when the wait exceeds
-// kWaitTimeoutNs, or as soon as another role of the CTA has aborted.
+// timeout_ns (kWaitTimeoutNs by default), or as soon as another role of the
+// CTA has aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int where) {
+                                          int where, uint64_t timeout_ns = kWaitTimeoutNs) {
   const uint32_t a = smem_addr(bar);
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t start = globaltimer_ns();
@@ -100,12 +101,30 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     if (mbar_try_wait(a, parity)) return true;
     if ((it & 31u) == 0) {
       if (*abort_flag) return false;
-      if (globaltimer_ns() - start > kWaitTimeoutNs) {
+      if (globaltimer_ns() - start > timeout_ns) {
         *abort_flag = 1;
         report_status(kStatusWaitTimeout, where);
         return false;
       }
     }
+  }
+}
+
+// Self-test of the bounded wait: one CTA waits on an mbarrier that nothing
+// will ever complete.  The wait must give up after timeout_ns, record
+// kStatusWaitTimeout (detail 99) and let the kernel return normally.
+__global__ void selftest_bounded_wait_kernel(uint64_t timeout_ns, int* waited_out) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const bool ok = mbar_wait(&bar, 0, &abort_flag, 99, timeout_ns);
+    *waited_out = ok ? 0 : 1;
   }
 }
 

@@ -303,6 +303,16 @@ int bokt_moe_topk_gate(const void* logits, int logits_dtype, int tokens, int E, 
 int bokt_moe_combine(const void* y, int64_t y_rows, const int32_t* rows, const float* gates,
                      void* out, int tokens, int k, int N, int dtype, void* stream);
 
+/*
+ * Failure-detection self-test: launches one CTA that waits on an mbarrier
+ * nothing will complete, with the same bounded wait every pipelined kernel
+ * uses.  After timeout_ns (<= 10 s) the wait gives up, the kernel writes 1 to
+ * the device int *gave_up, records code 1 / detail 99 in the device status
+ * word and returns; the CUDA context stays usable.  No counterpart in the
+ * reference.
+ */
+int bokt_selftest_bounded_wait(int64_t timeout_ns, int* gave_up, void* stream);
+
 /* Resource usage of the kernel a call with these arguments would launch. */
 int bokt_kernel_attrs(int kernel, int dtype, int n, int k, const bokt_params* params,
                       bokt_attrs* out);
