@@ -160,6 +160,39 @@ def graph_time_ms(stream, fn, count, reps=3):
     return best
 
 
+def paired_graph_times(stream, fn_a, fn_b, count=20, reps=9):
+    """Median per-step device time of two step functions, each captured as a
+    graph of ``count`` steps and replayed alternately (a, b, a, b, ...) so that
+    clock and power drift affect both alike; CUDA events on ``stream``."""
+    import statistics
+
+    import torch
+
+    graphs = []
+    for fn in (fn_a, fn_b):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(count):
+                fn(i)
+        graphs.append(g)
+    with torch.cuda.stream(stream):
+        for g in graphs:
+            g.replay()
+    torch.cuda.synchronize()
+    times = ([], [])
+    for _ in range(reps):
+        for g, out in zip(graphs, times):
+            b, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            b.record(stream)
+            with torch.cuda.stream(stream):
+                g.replay()
+            e.record(stream)
+            e.synchronize()
+            out.append(b.elapsed_time(e) / count)
+    del graphs
+    return statistics.median(times[0]), statistics.median(times[1])
+
+
 def cpu_threads():
     return os.cpu_count() or 1
 
@@ -331,6 +364,119 @@ class Gemm:
 
         numerics.gemm_fp32(self.ca, self.cb)  # BLAS threads
         return 2.0 * self.cpu_rows * self.size * self.n_local
+
+
+class RmsnormGemm:
+    """RMSNorm of x [4096, 4096] fused into the 4096 -> 14336 projection that
+    follows it (one kernel: norm-in-prologue tcgen05 GEMM); N split across
+    ranks with x replicated (no collective)."""
+
+    name = "rmsnorm_gemm"
+    unit = "TFLOP/s"
+    bound = "tensor"
+    dtype = "bf16"
+    launches_per_step = 2  # row-scale pass, row-scaled GEMM
+
+    def __init__(self, device, rank, world):
+        import torch
+
+        from flashattentionanycard_b200 import workloads
+        from flashattentionanycard_b200.configs.search_spaces import default_params
+
+        cfg = workloads.RMSNORM_GEMM
+        self.m, self.k, self.n, self.eps = cfg["m"], cfg["k"], cfg["n"], cfg["eps"]
+        if self.n % world:
+            raise SystemExit("N must divide evenly across ranks")
+        self.n_local = self.n // world
+        self.params = default_params("gemm")
+        self.norm_params = default_params("rmsnorm")
+        self.kernel = ("gemm_tc2_kernel<256,rowscale>" if self.params.get("CTA_GROUP") == 2
+                       else "gemm_tc_kernel<256,rowscale>")
+        from flashattentionanycard_b200.kernels import rmsnorm_gemm
+
+        x, w, b = workloads.rmsnorm_gemm_inputs(self.m, self.k, self.n, "bf16", seed=0,
+                                                device=device)
+        self.x, self.w = x, w
+        self.b = b[:, rank * self.n_local:(rank + 1) * self.n_local].contiguous()
+        # Weight preparation, once per (norm weight, B) pair: not part of a step.
+        self.b_folded = rmsnorm_gemm.fold_weight(w, self.b)
+        self.flops_per_step = 2.0 * self.m * self.k * self.n_local
+        per_set = (x.numel() + self.b.numel() + self.m * self.n_local) * 2
+        self.sets = max(1, math.ceil(ROTATION_BYTES / per_set)) if per_set < ROTATION_BYTES else 1
+        self.X = [x] + [x.roll(i, 0).contiguous() for i in range(1, self.sets)]
+        self.C = [torch.empty(self.m, self.n_local, device=device, dtype=x.dtype)
+                  for _ in range(self.sets)]
+        self.xn = torch.empty_like(x)
+        self.scales = torch.empty(self.m, device=device, dtype=torch.float32)
+
+    def step(self, i):
+        from flashattentionanycard_b200.kernels import rmsnorm_gemm
+
+        s = i % self.sets
+        rmsnorm_gemm.launch(self.X[s], self.b_folded, self.C[s], self.params, self.eps,
+                            scale_workspace=self.scales)
+
+    def dominant_kernel(self, i):
+        """The row-scaled GEMM alone (row factors from the last step's pass)."""
+        from flashattentionanycard_b200.kernels import rmsnorm_gemm
+
+        s = i % self.sets
+        rmsnorm_gemm.gemm_row_scaled(self.X[s], self.b_folded, self.C[s], self.scales,
+                                     self.params)
+
+    def unfused_step(self, i):
+        """The two-call chain the fused kernel replaces: rmsnorm, then GEMM."""
+        from flashattentionanycard_b200.kernels import gemm, rmsnorm
+
+        s = i % self.sets
+        rmsnorm.launch(self.X[s], self.w, self.xn, self.norm_params, self.eps)
+        gemm.launch(self.xn, self.b, self.C[s], self.params)
+
+    def config(self, world):
+        return {"workload": f"rmsnorm_gemm_bf16_{self.m}x{self.k}_to_{self.n}", "m": self.m,
+                "k": self.k, "n": self.n, "n_per_gpu": self.n_local, "eps": self.eps,
+                "partition": "N-split, x replicated, no collective",
+                "l2": "inputs > L2" if self.sets == 1 else f"rotating {self.sets} x/C sets",
+                "params": self.params}
+
+    def value(self, seconds_per_step, world):
+        return self.flops_per_step * world / seconds_per_step / 1e12
+
+    def e2e_setup(self):
+        import torch
+
+        # Per call the activations travel; the folded weight stays resident,
+        # as a layer's weights do.
+        self.h_in = [self.x.cpu().pin_memory()]
+        self.d_in = [[torch.empty_like(t, device=self.x.device) for t in self.h_in]
+                     for _ in range(2)]
+        self.d_out = [torch.empty(self.m, self.n_local, device=self.x.device, dtype=self.x.dtype)
+                      for _ in range(2)]
+        self.h_out = [torch.empty(self.m, self.n_local, dtype=self.x.dtype).pin_memory()
+                      for _ in range(2)]
+        self.h2d = sum(t.numel() * t.element_size() for t in self.h_in)
+        self.d2h = self.h_out[0].numel() * 2
+
+    def e2e_compute(self, b):
+        from flashattentionanycard_b200.kernels import rmsnorm_gemm
+
+        (x,) = self.d_in[b]
+        rmsnorm_gemm.launch(x, self.b_folded, self.d_out[b], self.params, self.eps)
+
+    def cpu_setup(self):
+        from flashattentionanycard_b200 import workloads
+
+        self.cpu_rows = 256
+        x, w, b = workloads.rmsnorm_gemm_inputs(self.m, self.k, self.n, "bf16", seed=0)
+        self.cx = x[: self.cpu_rows].float().numpy()
+        self.cw = w.float().numpy()
+        self.cb = b[:, : self.n_local].float().numpy()
+
+    def cpu_step(self, pool, threads):
+        from oracle import numerics
+
+        numerics.gemm_fp32(numerics.rmsnorm_fp32(self.cx, self.cw, self.eps), self.cb)
+        return 2.0 * self.cpu_rows * self.k * self.n_local
 
 
 class MoeSmall:
@@ -573,9 +719,10 @@ WORKLOADS = {
     "gemm2048": lambda d, r, w: Gemm(d, r, w, 2048, "bf16", split=False),
     "moe_small": lambda d, r, w: MoeSmall(d, r, w),
     "moe_large": lambda d, r, w: MoeLarge(d, r, w),
+    "rmsnorm_gemm": lambda d, r, w: RmsnormGemm(d, r, w),
 }
 DEFAULT_STEPS = {"rmsnorm": 4000, "gemm8192": 200, "gemm2048": 2000, "moe_small": 4000,
-                 "moe_large": 100}
+                 "moe_large": 100, "rmsnorm_gemm": 400}
 
 
 # ----------------------------------------------------------------------------- CPU reference
@@ -606,6 +753,9 @@ def cpu_sample_description(workload):
                 f" (K={workload.size})")
     if workload.name == "moe_small":
         return "numpy/BLAS fp32 per-expert GEMMs of the full 8-expert problem"
+    if workload.name == "rmsnorm_gemm":
+        return (f"numpy fp32 RMSNorm of {workload.cpu_rows} rows of x, then BLAS fp32 GEMM with "
+                f"B[:, :{workload.n_local}] (K={workload.k})")
     return "numpy/BLAS fp32 GEMM of 256 tokens x one expert's W[4096, 14336]"
 
 
@@ -679,6 +829,14 @@ def _cpu_only_workload(name):
         w.k, w.n = workloads.MOE_SMALL["k"], workloads.MOE_SMALL["n"]
         w.flops_per_step = 2.0 * sum(w.counts) * w.k * w.n
         w.cpu_config = lambda: {"workload": "moe_grouped_gemm_bf16_E8_K1024_N2048_T1528"}
+        return w
+    if name == "rmsnorm_gemm":
+        w = RmsnormGemm.__new__(RmsnormGemm)
+        cfg = workloads.RMSNORM_GEMM
+        w.m, w.k, w.n, w.eps = cfg["m"], cfg["k"], cfg["n"], cfg["eps"]
+        w.n_local = w.n
+        w.cpu_config = lambda: {"workload": f"rmsnorm_gemm_bf16_{w.m}x{w.k}_to_{w.n}",
+                                "sample": "256 rows of x per step"}
         return w
     w = CpuOnly()
     cfg = workloads.MOE_LARGE
@@ -836,7 +994,8 @@ def run_ours(args):
         kernel_ms = ms_per_step
         kernel_timing = "timed region / launches"
     else:
-        kernel_ms = graph_time_ms(stream, lambda i: _last_kernel(workload, i), 20)
+        dominant = getattr(workload, "dominant_kernel", None) or (lambda i: _last_kernel(workload, i))
+        kernel_ms = graph_time_ms(stream, dominant, 20)
         kernel_timing = "graph of 20 launches of the dominant kernel alone, best of 3"
     if workload.bound == "hbm" and workload.unit == "GB/s":
         achieved = workload.bytes_per_step / (kernel_ms / 1e3) / 1e9
@@ -851,6 +1010,16 @@ def run_ours(args):
         achieved = flops / (kernel_ms / 1e3) / 1e12
         peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
         unit_r = "TFLOP/s"
+    unfused = None
+    if hasattr(workload, "unfused_step"):
+        fused_ms, unfused_ms = paired_graph_times(stream, workload.step, workload.unfused_step)
+        unfused = {"ms_per_step": unfused_ms, "value": workload.value(unfused_ms / 1e3, world),
+                   "unit": workload.unit, "fused_ms_per_step": fused_ms,
+                   "fused_speedup": unfused_ms / fused_ms,
+                   "what": "the two-call chain replaced: rmsnorm.launch then gemm.launch "
+                           "(normalised x written to and read back from HBM)",
+                   "timing": "paired: graphs of 20 fused / 20 unfused steps replayed "
+                             "alternately 9 times each, medians"}
     traffic, traffic_source = profile_traffic(workload.name)
     roofline = {"kernel": workload.kernel, "bound": "hbm" if unit_r == "GB/s" else "tensor",
                 "achieved": achieved, "peak": peak, "unit": unit_r, "frac": achieved / peak,
@@ -915,6 +1084,8 @@ def run_ours(args):
         "e2e": e2e, "clocks": clocks, "gpu_launches": steps * workload.launches_per_step,
         "impl": "ours",
     }
+    if unfused is not None:
+        line["unfused"] = unfused
     print(json.dumps(line))
     return 0
 

@@ -15,7 +15,7 @@ LIBRARY_PATH = PACKAGE_DIR / "libbokt_sm100.so"
 ABI_VERSION = 1
 
 FP16, BF16 = 0, 1
-KERNEL_GEMM, KERNEL_RMSNORM, KERNEL_MOE_GROUPED_GEMM = 0, 1, 2
+KERNEL_GEMM, KERNEL_RMSNORM, KERNEL_MOE_GROUPED_GEMM, KERNEL_RMSNORM_GEMM = 0, 1, 2, 3
 
 ERRORS = {
     1: "invalid argument",
@@ -37,6 +37,7 @@ PARAM_FIELDS = {
     "ROWS_PER_CTA": "rows_per_cta",
     "SPLIT_K": "split_k",
     "CTA_GROUP": "cta_group",
+    "RASTER": "raster",
 }
 
 
@@ -52,7 +53,8 @@ class BoktParams(ctypes.Structure):
         ("rows_per_cta", ctypes.c_int32),
         ("split_k", ctypes.c_int32),
         ("cta_group", ctypes.c_int32),
-        ("reserved", ctypes.c_int32 * 6),
+        ("raster", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 5),
     ]
 
 
@@ -76,6 +78,10 @@ SIGNATURES = {
     "bokt_last_error": (ctypes.c_char_p, []),
     "bokt_gemm": (_I32, [_VP, _VP, _VP, _I32, _I32, _I32, _I32, _PP, _VP]),
     "bokt_rmsnorm": (_I32, [_VP, _VP, _VP, _I32, _I32, _F32, _I32, _PP, _VP]),
+    "bokt_rmsnorm_fold_weight": (_I32, [_VP, _VP, _VP, _I32, _I32, _I32, _VP]),
+    "bokt_rmsnorm_row_scale": (_I32, [_VP, _VP, _I32, _I32, _F32, _I32, _VP]),
+    "bokt_gemm_row_scaled": (_I32, [_VP, _VP, _VP, _VP, _I32, _I32, _I32, _I32, _PP, _VP]),
+    "bokt_rmsnorm_gemm": (_I32, [_VP, _VP, _VP, _VP, _I32, _I32, _I32, _F32, _I32, _PP, _VP]),
     "bokt_moe_grouped_gemm": (
         _I32,
         [_VP, _VP, _VP, _I32, _VP, _I32, _I32, _I32, _I32, _I32, _I32, _PP, _VP],

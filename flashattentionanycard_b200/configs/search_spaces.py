@@ -14,6 +14,9 @@ kernels:
   of the grouped GEMM (``sm_count * CTA_MULTIPLIER``).
 * GEMM only: ``CTA_GROUP`` 1 (one CTA per 128-row tile) or 2 (CTA pairs on two
   SMs, tcgen05 cta_group::2, 256-row tiles).
+* MoE grouped GEMM only: ``RASTER`` 1 walks the tiles expert by expert; 2 spreads
+  the tiles of experts with at most two 128-row blocks (weights read once or
+  twice: HBM-bound) evenly between the tiles of the others (tensor-bound).
 * RMSNorm: ``ROWS_PER_CTA`` and ``num_warps`` as in the reference, plus
   ``num_stages``: 1 keeps the reference's one-row-slice-per-CTA shape; 2 (with
   ROWS_PER_CTA 1) a persistent CTA per resident slot that keeps its next row's
@@ -98,6 +101,8 @@ def search_space(kernel: str, profile: str = "full") -> dict[str, list[int]]:
             space["CTA_GROUP"] = [1, 2]
     else:
         space["CTA_MULTIPLIER"] = [1, 2, 4] if profile == "full" else [1, 2]
+        if profile == "full":
+            space["RASTER"] = [1, 2]
     return space
 
 
@@ -109,7 +114,7 @@ def default_params(kernel: str) -> dict[str, int]:
     if kernel == "gemm":
         p.update(GROUP_M=8, CTA_GROUP=2, num_stages=6)
     else:
-        p["CTA_MULTIPLIER"] = 1
+        p.update(CTA_MULTIPLIER=1, RASTER=1)
     return p
 
 

@@ -16,6 +16,7 @@
 #include "gemm_tc.cuh"
 #include "gemm_tc2.cuh"
 #include "moe_route.cuh"
+#include "norm_gemm.cuh"
 #include "rmsnorm.cuh"
 
 namespace {
@@ -173,22 +174,26 @@ int encode_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dim
 // ----------------------------------------------------------------- GEMM dispatch
 using bokt::GemmTcArgs;
 
-template <int BN, bool GROUPED, typename T, bool SCATTER>
+template <int BN, bool GROUPED, typename T, bool SCATTER, bool NORM = false>
 const void* tc_kernel_ptr() {
-  return reinterpret_cast<const void*>(&bokt::gemm_tc_kernel<BN, GROUPED, T, SCATTER>);
+  return reinterpret_cast<const void*>(&bokt::gemm_tc_kernel<BN, GROUPED, T, SCATTER, NORM>);
 }
 
-template <bool GROUPED, typename T, bool SCATTER>
+template <bool GROUPED, typename T, bool SCATTER, bool NORM = false>
 const void* tc_kernel_for(int bn) {
   switch (bn) {
-    case 64: return tc_kernel_ptr<64, GROUPED, T, SCATTER>();
-    case 128: return tc_kernel_ptr<128, GROUPED, T, SCATTER>();
-    case 256: return tc_kernel_ptr<256, GROUPED, T, SCATTER>();
+    case 64: return tc_kernel_ptr<64, GROUPED, T, SCATTER, NORM>();
+    case 128: return tc_kernel_ptr<128, GROUPED, T, SCATTER, NORM>();
+    case 256: return tc_kernel_ptr<256, GROUPED, T, SCATTER, NORM>();
   }
   return nullptr;
 }
 
-const void* tc_kernel(bool grouped, int dtype, int bn, bool scatter = false) {
+const void* tc_kernel(bool grouped, int dtype, int bn, bool scatter = false,
+                      bool rowscale = false) {
+  if (rowscale)
+    return dtype == BOKT_BF16 ? tc_kernel_for<false, __nv_bfloat16, false, true>(bn)
+                              : tc_kernel_for<false, __half, false, true>(bn);
   if (scatter)
     return dtype == BOKT_BF16 ? tc_kernel_for<true, __nv_bfloat16, true>(bn)
                               : tc_kernel_for<true, __half, true>(bn);
@@ -200,7 +205,7 @@ const void* tc_kernel(bool grouped, int dtype, int bn, bool scatter = false) {
 }
 
 struct TcConfig {
-  int bn, stages, group_m, smem, cta_group;
+  int bn, stages, group_m, smem, cta_group, raster;
 };
 
 int resolve_tc_config(const bokt_params* p, bool grouped, int experts, int smem_optin,
@@ -223,6 +228,11 @@ int resolve_tc_config(const bokt_params* p, bool grouped, int experts, int smem_
     return fail(BOKT_ERR_UNSUPPORTED, "cta_group 2 is implemented for the dense GEMM only");
   if (cta_group == 2 && bn == 64)
     return fail(BOKT_ERR_CONFIG, "cta_group 2 needs block_n 128 or 256");
+  const int raster = param_or(p->raster, bokt::kRasterExpert);
+  if (raster != bokt::kRasterExpert && raster != bokt::kRasterBalanced)
+    return fail(BOKT_ERR_CONFIG, "raster must be 1 (expert order) or 2 (balanced)");
+  if (raster == bokt::kRasterBalanced && !grouped)
+    return fail(BOKT_ERR_CONFIG, "raster 2 applies to the grouped GEMM (dense: group_m)");
   const int stages = param_or(p->stages, cta_group == 2 ? (bn == 256 ? 6 : 8) : (bn == 256 ? 4 : 6));
   if (stages < 2 || stages > 8) return fail(BOKT_ERR_CONFIG, "stages must be in [2, 8]");
   int smem = cta_group == 2 ? bokt::gemm_tc2_smem_bytes(bn, stages)
@@ -239,10 +249,19 @@ int resolve_tc_config(const bokt_params* p, bool grouped, int experts, int smem_
   out->group_m = param_or(p->group_m, 8);
   out->smem = smem;
   out->cta_group = cta_group;
+  out->raster = raster;
   return BOKT_OK;
 }
 
-const void* tc2_kernel(int dtype, int bn) {
+const void* tc2_kernel(int dtype, int bn, bool rowscale = false) {
+  if (rowscale) {
+    if (dtype == BOKT_BF16)
+      return bn == 256
+                 ? reinterpret_cast<const void*>(&bokt::gemm_tc2_kernel<256, __nv_bfloat16, true>)
+                 : reinterpret_cast<const void*>(&bokt::gemm_tc2_kernel<128, __nv_bfloat16, true>);
+    return bn == 256 ? reinterpret_cast<const void*>(&bokt::gemm_tc2_kernel<256, __half, true>)
+                     : reinterpret_cast<const void*>(&bokt::gemm_tc2_kernel<128, __half, true>);
+  }
   if (dtype == BOKT_BF16)
     return bn == 256 ? reinterpret_cast<const void*>(&bokt::gemm_tc2_kernel<256, __nv_bfloat16>)
                      : reinterpret_cast<const void*>(&bokt::gemm_tc2_kernel<128, __nv_bfloat16>);
@@ -253,14 +272,15 @@ const void* tc2_kernel(int dtype, int bn) {
 // Dense GEMM on CTA pairs: cluster of 2 along x, PDL as every other launch.
 int launch_tc2(int dtype, const TcConfig& cfg, const CUtensorMap& ma, const CUtensorMap& mb,
                const GemmTcArgs& args, int pairs, cudaStream_t s) {
-  const void* fn = tc2_kernel(dtype, cfg.bn);
+  const void* fn = tc2_kernel(dtype, cfg.bn, args.row_scale != nullptr);
   int rc = ensure_smem(fn, cfg.smem);
   if (rc) return rc;
   void* kargs[] = {const_cast<CUtensorMap*>(&ma), const_cast<CUtensorMap*>(&mb),
                    const_cast<GemmTcArgs*>(&args)};
   cudaLaunchAttribute attr[2];
-  cudaLaunchConfig_t lc = launch_config(dim3(2 * pairs), dim3(bokt::kGemmThreads), cfg.smem, s,
-                                        attr);
+  cudaLaunchConfig_t lc = launch_config(
+      dim3(2 * pairs), dim3(bokt::kGemmThreads), cfg.smem, s,
+      attr);
   attr[lc.numAttrs].id = cudaLaunchAttributeClusterDimension;
   attr[lc.numAttrs].val.clusterDim.x = 2;
   attr[lc.numAttrs].val.clusterDim.y = 1;
@@ -274,7 +294,7 @@ int launch_tc2(int dtype, const TcConfig& cfg, const CUtensorMap& ma, const CUte
 int launch_tc(bool grouped, int dtype, const TcConfig& cfg, const CUtensorMap& ma,
               const CUtensorMap& mb, const GemmTcArgs& args, int grid, cudaStream_t s,
               bool scatter = false) {
-  const void* fn = tc_kernel(grouped, dtype, cfg.bn, scatter);
+  const void* fn = tc_kernel(grouped, dtype, cfg.bn, scatter, args.row_scale != nullptr);
   int rc = ensure_smem(fn, cfg.smem);
   if (rc) return rc;
   void* kargs[] = {const_cast<CUtensorMap*>(&ma), const_cast<CUtensorMap*>(&mb),
@@ -297,6 +317,61 @@ int launch_simt(const void* A, const void* B, void* C, int rows, int N, int K,
 
 bool tc_eligible(const void* A, const void* B, const void* C, int N, int K) {
   return K > 0 && (K % 8) == 0 && (N % 8) == 0 && aligned16(A) && aligned16(B) && aligned16(C);
+}
+
+// Dense GEMM entry body.  row_scale != nullptr scales C row m by row_scale[m]
+// in the epilogue (the fused RMSNorm -> GEMM; tcgen05 path only).
+int dense_gemm_impl(const void* A, const void* B, void* C, int M, int N, int K, int dtype,
+                    const bokt_params* params, void* stream, const float* row_scale) {
+  if (dtype != BOKT_FP16 && dtype != BOKT_BF16) return fail(BOKT_ERR_INVALID, "dtype %d", dtype);
+  if (M < 0 || N < 0 || K < 0) return fail(BOKT_ERR_INVALID, "negative size");
+  if (M == 0 || N == 0) return BOKT_OK;
+  if (!A || !B || !C) return fail(BOKT_ERR_INVALID, "null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  DeviceInfo dev;
+  int rc = device_info(&dev);
+  if (rc) return rc;
+  if (!tc_eligible(A, B, C, N, K)) {
+    if (row_scale)
+      return fail(BOKT_ERR_UNSUPPORTED,
+                  "fused RMSNorm-GEMM needs K > 0, K and N multiples of 8 and 16-byte aligned "
+                  "operands (got M=%d N=%d K=%d)", M, N, K);
+    return dtype == BOKT_BF16 ? launch_simt<__nv_bfloat16>(A, B, C, M, N, K, nullptr, 0, 0, s)
+                              : launch_simt<__half>(A, B, C, M, N, K, nullptr, 0, 0, s);
+  }
+  TcConfig cfg;
+  rc = resolve_tc_config(params, false, 0, dev.smem_optin, &cfg);
+  if (rc) return rc;
+  CUtensorMap ma, mb;
+  const uint64_t da[2] = {uint64_t(K), uint64_t(M)};
+  const uint64_t sa[1] = {uint64_t(K) * 2};
+  const uint32_t ba[2] = {64, 128};
+  rc = encode_map(&ma, A, 2, da, sa, ba, dtype == BOKT_FP16);
+  if (rc) return rc;
+  const uint64_t db[2] = {uint64_t(N), uint64_t(K)};
+  const uint64_t sb[1] = {uint64_t(N) * 2};
+  const uint32_t bb[2] = {64, 64};
+  rc = encode_map(&mb, B, 2, db, sb, bb, dtype == BOKT_FP16);
+  if (rc) return rc;
+  GemmTcArgs args = {};
+  args.C = C;
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.group_m = cfg.group_m;
+  args.stages = cfg.stages;
+  args.row_scale = row_scale;
+  if (cfg.cta_group == 2) {
+    args.idesc = bokt::make_idesc_f16(uint32_t(dtype), 256, uint32_t(cfg.bn));
+    const long long tiles2 = (long long)((M + 255) / 256) * ((N + cfg.bn - 1) / cfg.bn);
+    const long long max_pairs = dev.sm_count / 2;
+    const int pairs = int(tiles2 < max_pairs ? tiles2 : max_pairs);
+    return launch_tc2(dtype, cfg, ma, mb, args, pairs, s);
+  }
+  args.idesc = bokt::make_idesc_f16(uint32_t(dtype), 128, uint32_t(cfg.bn));
+  const long long tiles = (long long)((M + 127) / 128) * ((N + cfg.bn - 1) / cfg.bn);
+  const int grid = int(tiles < dev.sm_count ? tiles : dev.sm_count);
+  return launch_tc(false, dtype, cfg, ma, mb, args, grid, s);
 }
 
 // ----------------------------------------------------------------- RMSNorm dispatch
@@ -409,50 +484,82 @@ const char* bokt_last_error(void) { return g_err; }
 int bokt_gemm(const void* A, const void* B, void* C, int M, int N, int K, int dtype,
               const bokt_params* params, void* stream) {
   g_err[0] = 0;
+  return dense_gemm_impl(A, B, C, M, N, K, dtype, params, stream, nullptr);
+}
+
+int bokt_rmsnorm_fold_weight(const void* norm_weight, const void* B, void* B_folded, int K, int N,
+                             int dtype, void* stream) {
+  g_err[0] = 0;
   if (dtype != BOKT_FP16 && dtype != BOKT_BF16) return fail(BOKT_ERR_INVALID, "dtype %d", dtype);
-  if (M < 0 || N < 0 || K < 0) return fail(BOKT_ERR_INVALID, "negative size");
-  if (M == 0 || N == 0) return BOKT_OK;
-  if (!A || !B || !C) return fail(BOKT_ERR_INVALID, "null pointer");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (K < 0 || N < 0) return fail(BOKT_ERR_INVALID, "negative size");
+  if (K == 0 || N == 0) return BOKT_OK;
+  if (!norm_weight || !B || !B_folded) return fail(BOKT_ERR_INVALID, "null pointer");
+  if (N % 8 != 0 || !aligned16(B) || !aligned16(B_folded))
+    return fail(BOKT_ERR_UNSUPPORTED, "fold needs N %% 8 == 0 and 16-byte aligned B, B_folded");
   DeviceInfo dev;
   int rc = device_info(&dev);
   if (rc) return rc;
-  if (!tc_eligible(A, B, C, N, K)) {
-    return dtype == BOKT_BF16 ? launch_simt<__nv_bfloat16>(A, B, C, M, N, K, nullptr, 0, 0, s)
-                              : launch_simt<__half>(A, B, C, M, N, K, nullptr, 0, 0, s);
-  }
-  TcConfig cfg;
-  rc = resolve_tc_config(params, false, 0, dev.smem_optin, &cfg);
+  const long long vecs = (long long)K * (N / 8);
+  long long blocks = (vecs + 255) / 256;
+  if (blocks > 8LL * dev.sm_count) blocks = 8LL * dev.sm_count;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = dtype == BOKT_BF16
+      ? launch(bokt::fold_norm_weight_kernel<__nv_bfloat16>, dim3(unsigned(blocks)), dim3(256), 0, s,
+               static_cast<const __nv_bfloat16*>(norm_weight),
+               static_cast<const __nv_bfloat16*>(B), static_cast<__nv_bfloat16*>(B_folded), K, N)
+      : launch(bokt::fold_norm_weight_kernel<__half>, dim3(unsigned(blocks)), dim3(256), 0, s,
+               static_cast<const __half*>(norm_weight), static_cast<const __half*>(B),
+               static_cast<__half*>(B_folded), K, N);
+  if (e != cudaSuccess) return cuda_fail(e, "fold_norm_weight launch");
+  return BOKT_OK;
+}
+
+int bokt_rmsnorm_row_scale(const void* X, float* scale, int M, int K, float eps, int dtype,
+                           void* stream) {
+  g_err[0] = 0;
+  if (dtype != BOKT_FP16 && dtype != BOKT_BF16) return fail(BOKT_ERR_INVALID, "dtype %d", dtype);
+  if (M < 0 || K <= 0) return fail(BOKT_ERR_INVALID, "bad size");
+  if (M == 0) return BOKT_OK;
+  if (!X || !scale) return fail(BOKT_ERR_INVALID, "null pointer");
+  if (!(eps >= 0.f) || !(eps < 3.0e38f)) return fail(BOKT_ERR_INVALID, "eps must be finite >= 0");
+  if (K % 8 != 0 || !aligned16(X))
+    return fail(BOKT_ERR_UNSUPPORTED, "row scale needs K %% 8 == 0 and a 16-byte aligned X");
+  DeviceInfo dev;
+  int rc = device_info(&dev);
   if (rc) return rc;
-  CUtensorMap ma, mb;
-  const uint64_t da[2] = {uint64_t(K), uint64_t(M)};
-  const uint64_t sa[1] = {uint64_t(K) * 2};
-  const uint32_t ba[2] = {64, 128};
-  rc = encode_map(&ma, A, 2, da, sa, ba, dtype == BOKT_FP16);
+  const int warps = bokt::kRowScaleThreads / 32;
+  long long blocks = ((long long)M + warps - 1) / warps;
+  if (blocks > 16LL * dev.sm_count) blocks = 16LL * dev.sm_count;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = dtype == BOKT_BF16
+      ? launch(bokt::rmsnorm_row_scale_kernel<__nv_bfloat16>, dim3(unsigned(blocks)),
+               dim3(bokt::kRowScaleThreads), 0, s, static_cast<const __nv_bfloat16*>(X), scale, M,
+               K, eps)
+      : launch(bokt::rmsnorm_row_scale_kernel<__half>, dim3(unsigned(blocks)),
+               dim3(bokt::kRowScaleThreads), 0, s, static_cast<const __half*>(X), scale, M, K, eps);
+  if (e != cudaSuccess) return cuda_fail(e, "rmsnorm_row_scale launch");
+  return BOKT_OK;
+}
+
+int bokt_gemm_row_scaled(const void* A, const void* B, void* C, const float* row_scale, int M,
+                         int N, int K, int dtype, const bokt_params* params, void* stream) {
+  g_err[0] = 0;
+  if (!row_scale) return fail(BOKT_ERR_INVALID, "null row_scale");
+  return dense_gemm_impl(A, B, C, M, N, K, dtype, params, stream, row_scale);
+}
+
+int bokt_rmsnorm_gemm(const void* X, const void* B_folded, void* C, float* row_scale, int M,
+                      int N, int K, float eps, int dtype, const bokt_params* params,
+                      void* stream) {
+  g_err[0] = 0;
+  if (!row_scale) return fail(BOKT_ERR_INVALID, "null row_scale workspace");
+  if (M > 0 && N > 0 && !tc_eligible(X, B_folded, C, N, K))
+    return fail(BOKT_ERR_UNSUPPORTED,
+                "fused RMSNorm-GEMM needs K > 0, K and N multiples of 8 and 16-byte aligned "
+                "operands (got M=%d N=%d K=%d)", M, N, K);
+  int rc = bokt_rmsnorm_row_scale(X, row_scale, M, K, eps, dtype, stream);
   if (rc) return rc;
-  const uint64_t db[2] = {uint64_t(N), uint64_t(K)};
-  const uint64_t sb[1] = {uint64_t(N) * 2};
-  const uint32_t bb[2] = {64, 64};
-  rc = encode_map(&mb, B, 2, db, sb, bb, dtype == BOKT_FP16);
-  if (rc) return rc;
-  GemmTcArgs args = {};
-  args.C = C;
-  args.M = M;
-  args.N = N;
-  args.K = K;
-  args.group_m = cfg.group_m;
-  args.stages = cfg.stages;
-  if (cfg.cta_group == 2) {
-    args.idesc = bokt::make_idesc_f16(uint32_t(dtype), 256, uint32_t(cfg.bn));
-    const long long tiles2 = (long long)((M + 255) / 256) * ((N + cfg.bn - 1) / cfg.bn);
-    const long long max_pairs = dev.sm_count / 2;
-    const int pairs = int(tiles2 < max_pairs ? tiles2 : max_pairs);
-    return launch_tc2(dtype, cfg, ma, mb, args, pairs, s);
-  }
-  args.idesc = bokt::make_idesc_f16(uint32_t(dtype), 128, uint32_t(cfg.bn));
-  const long long tiles = (long long)((M + 127) / 128) * ((N + cfg.bn - 1) / cfg.bn);
-  const int grid = int(tiles < dev.sm_count ? tiles : dev.sm_count);
-  return launch_tc(false, dtype, cfg, ma, mb, args, grid, s);
+  return dense_gemm_impl(X, B_folded, C, M, N, K, dtype, params, stream, row_scale);
 }
 
 }  // extern "C"
@@ -514,6 +621,7 @@ int grouped_gemm_impl(const void* X, const void* W, const void* offsets, int off
   args.offsets = offsets;
   args.offsets_i64 = offsets_is_i64 ? 1 : 0;
   args.E = E;
+  args.raster = cfg.raster;
   if (scatter) {
     args.rowmap = scatter->rowmap;
     args.out_ptrs = scatter->out_ptrs;
@@ -915,16 +1023,21 @@ int bokt_kernel_attrs(int kernel, int dtype, int n, int k, const bokt_params* pa
   if (rc) return rc;
   const void* fn = nullptr;
   int dyn = 0, threads = 0, path = 0;
-  if (kernel == BOKT_KERNEL_GEMM || kernel == BOKT_KERNEL_MOE_GROUPED_GEMM) {
+  if (kernel == BOKT_KERNEL_GEMM || kernel == BOKT_KERNEL_MOE_GROUPED_GEMM ||
+      kernel == BOKT_KERNEL_RMSNORM_GEMM) {
     const bool grouped = kernel == BOKT_KERNEL_MOE_GROUPED_GEMM;
+    const bool norm = kernel == BOKT_KERNEL_RMSNORM_GEMM;
     if ((n % 8) == 0 && (k % 8) == 0 && k > 0) {
       TcConfig cfg;
       rc = resolve_tc_config(params, grouped, grouped ? 64 : 0, dev.smem_optin, &cfg);
       if (rc) return rc;
-      fn = cfg.cta_group == 2 ? tc2_kernel(dtype, cfg.bn) : tc_kernel(grouped, dtype, cfg.bn);
+      fn = cfg.cta_group == 2 ? tc2_kernel(dtype, cfg.bn, norm)
+                              : tc_kernel(grouped, dtype, cfg.bn, false, norm);
       dyn = cfg.smem;
       threads = bokt::kGemmThreads;
       path = 0;
+    } else if (norm) {
+      return fail(BOKT_ERR_UNSUPPORTED, "fused RMSNorm-GEMM needs K and N multiples of 8");
     } else {
       fn = dtype == BOKT_BF16 ? reinterpret_cast<const void*>(&bokt::gemm_simt_kernel<__nv_bfloat16>)
                               : reinterpret_cast<const void*>(&bokt::gemm_simt_kernel<__half>);

@@ -45,7 +45,19 @@ struct GemmTcArgs {
   void* const* out_ptrs;
   int rows_per_owner;
   int owners;
+  // Dense only, or null: C row m is scaled by row_scale[m] in the fp32
+  // epilogue before rounding (the RMSNorm row factor of the fused
+  // RMSNorm -> GEMM, whose norm weight is folded into B).
+  const float* row_scale;
+  // Grouped tile order: kRasterExpert walks experts in index order (M fastest
+  // inside an expert); kRasterBalanced spreads the tiles of low-reuse experts
+  // (at most kLowReuseMBlocks row blocks) evenly between the others.
+  int raster;
 };
+
+constexpr int kRasterExpert = 1;
+constexpr int kRasterBalanced = 2;
+constexpr int kLowReuseMBlocks = 2;
 
 template <int BN>
 struct GemmTcShape {
@@ -65,7 +77,7 @@ constexpr int kEpiBytes = kEpiWarps * (kEpiStageBytes + 32 * 8);
 __host__ __device__ inline int gemm_tc_smem_bytes(int bn, int stages, bool grouped, int experts) {
   int bytes = 1024 /* alignment slack */ + stages * (kGemmABytes + bn * kGemmBK * 2) +
               kEpiBytes + (2 * stages + 4) * 8 + 16;
-  if (grouped) bytes += (3 * experts + 1) * 4;
+  if (grouped) bytes += (4 * experts + 4) * 4;
   return bytes;
 }
 
@@ -76,10 +88,10 @@ __host__ __device__ inline int gemm_tc_smem_bytes(int bn, int stages, bool group
 // is written back with every group of 8 lanes storing one full 128-byte row
 // segment: coalesced HBM writes, and full-line NVLink writes when a row
 // pointer is a peer GPU's memory.
-template <int BN, typename OutT>
+template <int BN, typename OutT, bool SCALED = false>
 __device__ __forceinline__ void epilogue_store_tile(uint32_t taddr, uint8_t* stage,
                                                     OutT* const* rowptr, int n0, int N,
-                                                    int lane) {
+                                                    int lane, float scale = 1.f) {
 #pragma unroll 1
   for (int c = 0; c < BN; c += 64) {
     uint32_t v0[32], v1[32];
@@ -89,8 +101,12 @@ __device__ __forceinline__ void epilogue_store_tile(uint32_t taddr, uint8_t* sta
     uint8_t* my_row = stage + lane * 128;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const uint32_t* v = j < 4 ? v0 : v1;
+      uint32_t* v = j < 4 ? v0 : v1;
       const int b = (j & 3) * 8;
+      if constexpr (SCALED) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[b + e] = __float_as_uint(__uint_as_float(v[b + e]) * scale);
+      }
       uint4 pk;
       pk.x = Pack2<OutT>::pack(__uint_as_float(v[b + 0]), __uint_as_float(v[b + 1]));
       pk.y = Pack2<OutT>::pack(__uint_as_float(v[b + 2]), __uint_as_float(v[b + 3]));
@@ -139,34 +155,143 @@ __device__ __forceinline__ TileCoord dense_tile(int t, int M, int nn, int group_
   return c;
 }
 
-__device__ __forceinline__ TileCoord grouped_tile(int t, const int* tile_prefix,
-                                                  const int* row_start, const int* row_count,
-                                                  int E, int nn, int bn) {
-  // Largest e with tile_prefix[e] <= t (tile_prefix is non-decreasing, t < tile_prefix[E]).
+// Grouped schedule in shared memory, built once per CTA from the device offsets.
+// Experts are listed in schedule order (pos): the high-reuse experts first, in
+// index order, then the low-reuse ones; pre[pos] is the first tile of that
+// entry in the concatenated tile sequence.  With kRasterExpert every expert is
+// high-reuse, so the sequence is the plain index order.
+struct GroupedSchedule {
+  int* pre;      // [E+1] tile prefix over schedule positions
+  int* pstart;   // [E]   first packed row of the entry's expert
+  int* pcount;   // [E]   rows of the entry's expert
+  int* pexp;     // [E]   expert index of the entry
+  int* totals;   // [3]   all tiles, low-reuse tiles, high-reuse entries
+};
+
+__device__ __forceinline__ void expert_rows(const GemmTcArgs& args, int e, int* start, int* count) {
+  long long s, t;
+  if (args.offsets_i64) {
+    s = reinterpret_cast<const long long*>(args.offsets)[e];
+    t = reinterpret_cast<const long long*>(args.offsets)[e + 1];
+  } else {
+    s = reinterpret_cast<const int*>(args.offsets)[e];
+    t = reinterpret_cast<const int*>(args.offsets)[e + 1];
+  }
+  const long long T = args.M;
+  s = s < 0 ? 0 : (s > T ? T : s);
+  t = t < s ? s : (t > T ? T : t);
+  *start = static_cast<int>(s);
+  *count = static_cast<int>(t - s);
+}
+
+// Build the schedule with every thread of the CTA.  `scratch` holds 4 ints per
+// thread.  Ends with the schedule complete but without a barrier after it.
+__device__ __forceinline__ void build_grouped_schedule(const GemmTcArgs& args, int nn,
+                                                       const GroupedSchedule& g, int* scratch) {
+  const int E = args.E;
+  const int nt = blockDim.x;
+  const int per = (E + nt - 1) / nt;
+  const int e0 = min(E, static_cast<int>(threadIdx.x) * per);
+  const int e1 = min(E, e0 + per);
+  const bool balanced = args.raster == kRasterBalanced;
+  int he = 0, le = 0, ht = 0, lt = 0;
+  for (int e = e0; e < e1; ++e) {
+    int st, c;
+    expert_rows(args, e, &st, &c);
+    const int mb = (c + kGemmBM - 1) / kGemmBM;
+    if (balanced && mb <= kLowReuseMBlocks) {
+      ++le;
+      lt += mb * nn;
+    } else {
+      ++he;
+      ht += mb * nn;
+    }
+  }
+  int* mine = scratch + 4 * threadIdx.x;
+  mine[0] = he;
+  mine[1] = le;
+  mine[2] = ht;
+  mine[3] = lt;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc[4] = {0, 0, 0, 0};
+    for (int i = 0; i < nt; ++i) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int v = scratch[4 * i + j];
+        scratch[4 * i + j] = acc[j];
+        acc[j] += v;
+      }
+    }
+    g.totals[0] = acc[2] + acc[3];
+    g.totals[1] = acc[3];
+    g.totals[2] = acc[0];
+    g.pre[E] = acc[2] + acc[3];
+  }
+  __syncthreads();
+  int hpos = mine[0];
+  int lpos = g.totals[2] + mine[1];
+  int htile = mine[2];
+  int ltile = (g.totals[0] - g.totals[1]) + mine[3];
+  for (int e = e0; e < e1; ++e) {
+    int st, c;
+    expert_rows(args, e, &st, &c);
+    const int mb = (c + kGemmBM - 1) / kGemmBM;
+    int pos;
+    if (balanced && mb <= kLowReuseMBlocks) {
+      pos = lpos++;
+      g.pre[pos] = ltile;
+      ltile += mb * nn;
+    } else {
+      pos = hpos++;
+      g.pre[pos] = htile;
+      htile += mb * nn;
+    }
+    g.pstart[pos] = st;
+    g.pcount[pos] = c;
+    g.pexp[pos] = e;
+  }
+}
+
+__device__ __forceinline__ TileCoord grouped_tile(int t, const GroupedSchedule& g, int E, int nn,
+                                                  int bn, int raster, bool* low) {
+  const int total = g.totals[0];
+  const int nlow = g.totals[1];
+  int u = t;
+  if (raster == kRasterBalanced && nlow > 0) {
+    // Position t of the sequence is a low-reuse tile iff floor((t+1) nlow / total)
+    // steps up there: the nlow low-reuse tiles are spread evenly, both
+    // subsequences keep their order.
+    const int f0 = static_cast<int>(static_cast<long long>(t) * nlow / total);
+    const int f1 = static_cast<int>(static_cast<long long>(t + 1) * nlow / total);
+    u = f1 > f0 ? (total - nlow) + f0 : t - f0;
+  }
+  // Largest pos with pre[pos] <= u (pre is non-decreasing, u < pre[E]); empty
+  // experts share their successor's prefix and are skipped by taking the last.
   int lo = 0, hi = E - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
-    if (tile_prefix[mid] <= t) lo = mid;
+    if (g.pre[mid] <= u) lo = mid;
     else hi = mid - 1;
   }
-  const int e = lo;
-  const int rel = t - tile_prefix[e];
-  const int count = row_count[e];
+  const int rel = u - g.pre[lo];
+  const int count = g.pcount[lo];
   const int mblocks = (count + kGemmBM - 1) / kGemmBM;
   // M fastest inside an expert: all row blocks of one weight column block run
   // together, so W[e][:, n-block] is fetched from HBM once and reused from L2.
   const int mb = rel % mblocks;
   const int nb = rel / mblocks;
   TileCoord c;
-  c.a_row = row_start[e] + mb * kGemmBM;
+  c.a_row = g.pstart[lo] + mb * kGemmBM;
   c.n0 = nb * bn;
-  c.expert = e;
+  c.expert = g.pexp[lo];
   c.c_row = c.a_row;
   c.rows_valid = min(kGemmBM, count - mb * kGemmBM);
+  *low = lo >= g.totals[2];
   return c;
 }
 
-template <int BN, bool GROUPED, typename OutT, bool SCATTER = false>
+template <int BN, bool GROUPED, typename OutT, bool SCATTER = false, bool ROWSCALE = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    GemmTcArgs args) {
@@ -185,9 +310,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  int* tile_prefix = reinterpret_cast<int*>(tmem_holder + 4);  // [E+1], grouped only
-  int* row_start = tile_prefix + (args.E + 1);                 // [E]
-  int* row_count = row_start + args.E;                         // [E]
+  GroupedSchedule sched;  // grouped only: [E+1] + 3 x [E] + [3] ints
+  sched.pre = reinterpret_cast<int*>(tmem_holder + 4);
+  sched.pstart = sched.pre + (args.E + 1);
+  sched.pcount = sched.pstart + args.E;
+  sched.pexp = sched.pcount + args.E;
+  sched.totals = sched.pexp + args.E;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -221,43 +349,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   int ntiles;
   if constexpr (GROUPED) {
-    const int E = args.E;
-    const int T = args.M;
-    for (int e = threadIdx.x; e < E; e += blockDim.x) {
-      long long s, t;
-      if (args.offsets_i64) {
-        s = reinterpret_cast<const long long*>(args.offsets)[e];
-        t = reinterpret_cast<const long long*>(args.offsets)[e + 1];
-      } else {
-        s = reinterpret_cast<const int*>(args.offsets)[e];
-        t = reinterpret_cast<const int*>(args.offsets)[e + 1];
-      }
-      s = s < 0 ? 0 : (s > T ? T : s);
-      t = t < s ? s : (t > T ? T : t);
-      row_start[e] = static_cast<int>(s);
-      row_count[e] = static_cast<int>(t - s);
-      tile_prefix[e + 1] = static_cast<int>((t - s + kGemmBM - 1) / kGemmBM) * nn;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      tile_prefix[0] = 0;
-      for (int e = 0; e < E; ++e) tile_prefix[e + 1] += tile_prefix[e];
-    }
+    // The epilogue staging area is free until the first tile: scratch for the scan.
+    build_grouped_schedule(args, nn, sched, reinterpret_cast<int*>(sEpi));
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   if constexpr (GROUPED) {
-    ntiles = tile_prefix[args.E];
+    ntiles = sched.totals[0];
   } else {
     ntiles = ((args.M + kGemmBM - 1) / kGemmBM) * nn;
   }
 
-  auto tile_at = [&](int t) -> TileCoord {
+  auto tile_at = [&](int t, bool* low) -> TileCoord {
     if constexpr (GROUPED) {
-      return grouped_tile(t, tile_prefix, row_start, row_count, args.E, nn, BN);
+      return grouped_tile(t, sched, args.E, nn, BN, args.raster, low);
     } else {
+      *low = false;
       return dense_tile(t, args.M, nn, args.group_m, BN);
     }
   };
@@ -268,8 +377,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      const uint64_t evict_first = l2_policy_evict_first();
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-        const TileCoord tc = tile_at(t);
+        bool low;
+        const TileCoord tc = tile_at(t, &low);
         for (int kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, 1)) {
             ok = false;
@@ -282,8 +393,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int c = 0; c < BN / 64; ++c) {
             if constexpr (GROUPED) {
-              tma_load_3d(b_dst + c * 8192, &tmB, &full[stage], tc.n0 + c * 64, kb * kGemmBK,
-                          tc.expert);
+              // Weights of a low-reuse expert are read by at most two tiles:
+              // stream them past L2 residents.
+              if (low) {
+                tma_load_3d_hint(b_dst + c * 8192, &tmB, &full[stage], tc.n0 + c * 64,
+                                 kb * kGemmBK, tc.expert, evict_first);
+              } else {
+                tma_load_3d(b_dst + c * 8192, &tmB, &full[stage], tc.n0 + c * 64, kb * kGemmBK,
+                            tc.expert);
+              }
             } else {
               tma_load_2d(b_dst + c * 8192, &tmB, &full[stage], tc.n0 + c * 64, kb * kGemmBK);
             }
@@ -344,7 +462,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     OutT** rowptr = reinterpret_cast<OutT**>(sEpi + kEpiWarps * kEpiStageBytes) + (warp - 2) * 32;
     int i = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
-      const TileCoord tc = tile_at(t);
+      bool low;
+      const TileCoord tc = tile_at(t, &low);
       const int acc = i & 1;
       const uint32_t acc_phase = (static_cast<uint32_t>(i) >> 1) & 1u;
       const bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, 4);
@@ -368,8 +487,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
       rowptr[lane] = row_ok ? crow : nullptr;
+      float scale = 1.f;
+      if constexpr (ROWSCALE) scale = row_ok ? args.row_scale[tc.c_row + r] : 1.f;
       __syncwarp();
-      epilogue_store_tile<BN, OutT>(taddr, stage, rowptr, tc.n0, N, lane);
+      epilogue_store_tile<BN, OutT, ROWSCALE>(taddr, stage, rowptr, tc.n0, N, lane, scale);
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
     }

@@ -35,7 +35,9 @@ __host__ __device__ inline int gemm_tc2_smem_bytes(int bn, int stages) {
          (2 * stages + 4) * 8 + 16;
 }
 
-template <int BN, typename OutT>
+// ROWSCALE: the epilogue scales C row m by args.row_scale[m] (fp32) before
+// rounding (fused RMSNorm -> GEMM with the norm weight folded into B).
+template <int BN, typename OutT, bool ROWSCALE = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     GemmTcArgs args) {
@@ -192,8 +194,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const int row = m0 + static_cast<int>(rank) * kGemmBM + r;
       rowptr[lane] = row < M ? C + static_cast<size_t>(row) * N + n0 : nullptr;
+      float scale = 1.f;
+      if constexpr (ROWSCALE) scale = row < M ? args.row_scale[row] : 1.f;
       __syncwarp();
-      epilogue_store_tile<BN, OutT>(taddr, stage, rowptr, n0, N, lane);
+      epilogue_store_tile<BN, OutT, ROWSCALE>(taddr, stage, rowptr, n0, N, lane, scale);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(map_shared(smem_addr(&tempty[acc]), 0));

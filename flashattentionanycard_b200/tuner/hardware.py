@@ -114,7 +114,7 @@ def gemm_shared_bytes(block_n, stages, experts=0):
     b_bytes = block_n * GEMM_BK * 2
     total = 1024 + stages * (a_bytes + b_bytes) + EPILOGUE_BYTES + (2 * stages + 4) * 8 + 16
     if experts:
-        total += (3 * experts + 1) * 4
+        total += (4 * experts + 4) * 4
     return total
 
 

@@ -22,6 +22,9 @@ MOE_SMALL_COUNTS = (0, 16, 64, 256, 1024, 32, 8, 128)
 MOE_SMALL = {"experts": 8, "k": 1024, "n": 2048}
 MOE_LARGE = {"experts": 64, "k": 4096, "n": 14336, "tokens": 16384, "topk": 2, "zipf_s": 1.1}
 RMSNORM = {"m": 4096, "n": 4096, "eps": 1e-6}
+# RMSNorm of the 4096 x 4096 activations feeding a 4096 -> 14336 projection
+# (the MoE expert shape): the fused norm-in-prologue GEMM.
+RMSNORM_GEMM = {"m": 4096, "k": 4096, "n": 14336, "eps": 1e-6}
 
 
 def _torch_dtype(dtype):
@@ -121,3 +124,13 @@ def moe_large_inputs(dtype="bf16", seed=0, device="cuda", tokens=None, experts=N
     for e in range(experts):
         w[e] = (0.02 * torch.randn((k, n), generator=g, device=device, dtype=torch.float32)).to(dt)
     return x, w, ids
+
+
+def rmsnorm_gemm_inputs(m, k, n, dtype="bf16", seed=0, device="cpu"):
+    """x [m, k] ~ N(0, 1), norm weight [k] ~ N(1, 0.1), B [k, n] ~ N(0, 1) * k^-0.5."""
+    import torch
+
+    x, w = rmsnorm_inputs(m, k, dtype, seed, device)
+    g = _gen(device, seed + 1)
+    b = torch.randn((k, n), generator=g, device=device, dtype=torch.float32) / math.sqrt(k)
+    return x, w, b.to(_torch_dtype(dtype))

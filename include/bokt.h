@@ -21,6 +21,10 @@
  *                              expert token counts -> offsets); the permutation and combine
  *                              indices have no counterpart in the reference
  *                              (kernels/moe_grouped_gemm.py:3 leaves routing outside)
+ *   bokt_rmsnorm_gemm       <- the two calls rmsnorm.launch(x, w, xn) then gemm.launch(xn, b, out)
+ *   (+ _fold_weight,           (kernels/rmsnorm.py:29-33 followed by kernels/gemm.py:43-48),
+ *    _row_scale,               fused: the normalised activations never reach HBM
+ *    bokt_gemm_row_scaled)
  *   bokt_gather_rows        <- no counterpart (packing tokens in expert order)
  *   bokt_kernel_attrs       <- the Triton compiled-kernel metadata read by
  *                              bo_kernel_tuner/tuner/worker.py:193,203-204
@@ -54,6 +58,7 @@ extern "C" {
 #define BOKT_KERNEL_GEMM 0
 #define BOKT_KERNEL_RMSNORM 1
 #define BOKT_KERNEL_MOE_GROUPED_GEMM 2
+#define BOKT_KERNEL_RMSNORM_GEMM 3
 
 /*
  * Launch parameters: the CUDA counterpart of the Triton meta-parameters the
@@ -67,6 +72,11 @@ extern "C" {
  *   RMSNorm             : rows_per_cta, num_warps; stages >= 2 selects the persistent
  *                         ring kernel (stages row buffers, num_warps consumer warps)
  *   GEMM                : cta_group 2 runs CTA pairs (tcgen05 cta_group::2, 256-row tiles)
+ *   grouped GEMM        : raster 1 (the default) runs the tiles expert by expert;
+ *                         raster 2 spreads the tiles of experts with at most two
+ *                         128-row blocks evenly between the others, so their
+ *                         once-read weights stream (L2 evict-first) while other
+ *                         tiles compute
  */
 typedef struct bokt_params {
   int32_t block_m;
@@ -79,7 +89,9 @@ typedef struct bokt_params {
   int32_t rows_per_cta;
   int32_t split_k;   /* reserved: must be 0 or 1 */
   int32_t cta_group; /* 0/1: one CTA per tile; 2: CTA pairs (dense GEMM) */
-  int32_t reserved[6];
+  int32_t raster;    /* grouped GEMM tile order: 0/1 expert order, 2 balanced
+                        (low-reuse experts spread between the others) */
+  int32_t reserved[5];
 } bokt_params;
 
 typedef struct bokt_attrs {
@@ -114,6 +126,29 @@ int bokt_gemm(const void* A, const void* B, void* C, int M, int N, int K, int dt
  */
 int bokt_rmsnorm(const void* X, const void* W, void* Y, int M, int N, float eps, int dtype,
                  const bokt_params* params, void* stream);
+
+/*
+ * Fused RMSNorm -> GEMM.  The reference chain rmsnorm.launch(x, w, xn) then
+ * gemm.launch(xn, B, out) is computed as
+ *   out[m, :] = s[m] * (X[m, :] @ B_folded),   B_folded[k, n] = w[k] * B[k, n],
+ *   s[m] = rsqrt(sum_k X[m, k]^2 / K + eps),
+ * with s applied to the fp32 accumulator in the tcgen05 GEMM epilogue: the
+ * normalised activations never reach HBM.  The fold is done once per (w, B)
+ * pair with bokt_rmsnorm_fold_weight; each call of bokt_rmsnorm_gemm runs the
+ * one-pass row-scale kernel (reads X once; scales into the caller's row_scale
+ * workspace of M floats) and the row-scaled GEMM (same params as bokt_gemm).
+ * Needs K and N multiples of 8 and 16-byte aligned pointers (else
+ * BOKT_ERR_UNSUPPORTED).
+ */
+int bokt_rmsnorm_fold_weight(const void* norm_weight, const void* B, void* B_folded, int K, int N,
+                             int dtype, void* stream);
+int bokt_rmsnorm_row_scale(const void* X, float* row_scale, int M, int K, float eps, int dtype,
+                           void* stream);
+int bokt_gemm_row_scaled(const void* A, const void* B, void* C, const float* row_scale, int M,
+                         int N, int K, int dtype, const bokt_params* params, void* stream);
+int bokt_rmsnorm_gemm(const void* X, const void* B_folded, void* C, float* row_scale, int M,
+                      int N, int K, float eps, int dtype, const bokt_params* params,
+                      void* stream);
 
 /*
  * For each expert e: Y[off[e]:off[e+1]] = X[off[e]:off[e+1]] * W[e], W of shape

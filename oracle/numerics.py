@@ -62,6 +62,21 @@ def rmsnorm_fp32(x, weight, eps):
     return (x * inv) * np.asarray(weight, dtype=np.float32)
 
 
+def rmsnorm_gemm_fp32(x, weight, b, eps):
+    """The two-operator chain ``rmsnorm(x, w)`` (reference worker.py:73-74)
+    followed by ``@ b`` (worker.py:64), in fp32 with no intermediate rounding:
+    the answer the fused RMSNorm -> GEMM is gated against."""
+    return gemm_fp32(rmsnorm_fp32(x, weight, eps), b)
+
+
+def rmsnorm_row_scale_fp32(x, eps):
+    """Per-row ``rsqrt(mean(x^2) + eps)`` in fp32: the factor rmsnorm_fp32
+    multiplies each row by before the weight (reference worker.py:73-74)."""
+    x = np.asarray(x, dtype=np.float32)
+    mean_sq = np.mean(np.square(x), axis=-1, dtype=np.float32)
+    return (np.float32(1.0) / np.sqrt(mean_sq + np.float32(eps))).astype(np.float32)
+
+
 def grouped_gemm_fp32(x, weights, offsets):
     """Per-expert ``x[s_e:s_{e+1}] @ W[e]`` concatenated (reference worker.py:88-90).
 

@@ -140,6 +140,32 @@ def test_tcgen05_grouped_gemm_ragged_experts(counts, offset_dtype, cuda_device):
         gate(out, ref, "bf16")
 
 
+@pytest.mark.parametrize("experts", [191, 193, 300, 1000])
+def test_grouped_gemm_balanced_raster_many_experts(experts, cuda_device):
+    """RASTER 2 (low-reuse experts interleaved) computes the same tiles as
+    RASTER 1, bit for bit, with the schedule scan spread over every thread."""
+    n, k = 136, 72
+    rng = np.random.default_rng(experts)
+    counts = rng.integers(0, 400, size=experts)
+    counts[rng.integers(0, experts, size=experts // 5)] = 0
+    starts = np.concatenate([[0], np.cumsum(counts)]).tolist()
+    g = torch.Generator().manual_seed(experts)
+    x = torch.randn(starts[-1], k, generator=g).bfloat16()
+    w = (0.5 * torch.randn(experts, k, n, generator=g)).bfloat16()
+    ref = numerics.grouped_gemm_fp32(as_f32(x), as_f32(w), starts)
+    xd, wd = x.to(cuda_device), w.to(cuda_device)
+    offsets = torch.tensor(starts, dtype=torch.int32, device=cuda_device)
+    outs = []
+    for raster in (1, 2):
+        out = nan_like((x.shape[0], n), "bf16", cuda_device)
+        moe_grouped_gemm.launch(xd, wd, offsets, out,
+                                {"BLOCK_N": 128, "num_stages": 4, "RASTER": raster}, 148)
+        torch.cuda.synchronize()
+        gate(out, ref, "bf16")
+        outs.append(out)
+    assert torch.equal(outs[0], outs[1])
+
+
 def test_grouped_gemm_leaves_rows_outside_experts(cuda_device):
     """Rows before offsets[0] and after offsets[E] are not written (reference
     kernel writes only [start, start + count) per expert)."""

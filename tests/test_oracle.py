@@ -129,3 +129,21 @@ def test_combine_oracle():
     assert np.allclose(out, [[1, 2], [4, 5], [0.25 * 8 + 0.75 * 10, 0.25 * 9 + 0.75 * 11]])
     perm_rows = np.array([5, 4, 3, 2, 1, 0])
     assert np.allclose(routing.combine(y, gates, perm_rows)[0], 0.5 * y[5] + 0.5 * y[4])
+
+
+def test_fused_rmsnorm_gemm_restatement_is_exact_algebra():
+    """The fused operator computes s[m] * (x[m] @ (w * b)) with s the per-row
+    RMSNorm factor: in exact (float64) arithmetic this is the reference chain
+    rmsnorm(x, w) @ b, so only the roundings differ."""
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((33, 40))
+    w = 1 + 0.1 * rng.standard_normal(40)
+    b = rng.standard_normal((40, 24)) / np.sqrt(40)
+    eps = 1e-6
+    chain = (x / np.sqrt(np.mean(x * x, axis=1, keepdims=True) + eps) * w) @ b
+    s = 1 / np.sqrt(np.mean(x * x, axis=1) + eps)
+    fused = s[:, None] * (x @ (w[:, None] * b))
+    np.testing.assert_allclose(fused, chain, rtol=1e-12, atol=1e-12)
+    ref32 = numerics.rmsnorm_gemm_fp32(x, w, b, eps)
+    np.testing.assert_allclose(ref32, chain, rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(numerics.rmsnorm_row_scale_fp32(x, eps), s, rtol=1e-6)
