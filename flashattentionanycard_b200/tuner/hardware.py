@@ -13,6 +13,7 @@ Mirrors the reference's ``bo_kernel_tuner/tuner/hardware.py`` (``Hardware``
   an optional, stricter pre-filter against the per-block limit.
 """
 
+import re
 import subprocess
 from dataclasses import asdict, dataclass, field
 
@@ -69,7 +70,9 @@ def parse_topology(text):
     """Parse ``nvidia-smi topo -m`` output into {gpu_index: {peer_index: link}}.
 
     ``link`` is the matrix entry, e.g. ``NV18`` (18 NVLinks through NVSwitch),
-    ``SYS``, ``PIX`` or ``X`` (self)."""
+    ``SYS``, ``PIX`` or ``X`` (self).  nvidia-smi underlines the header row with
+    terminal escape sequences; they are removed before the columns are matched."""
+    text = re.sub(r"\x1b\[[0-9;]*m", "", text)
     rows = [line.split() for line in text.splitlines() if line.strip()]
     if not rows:
         return {}

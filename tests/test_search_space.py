@@ -92,6 +92,22 @@ NIC0\tSYS\tSYS\tSYS\t X
 """
 
 
+def test_topology_header_with_terminal_escapes():
+    """nvidia-smi prints the header row underlined (ESC[4m ... ESC[0m)."""
+    text = ("\t\x1b[4mGPU0\tGPU1\tCPU Affinity\tNUMA Affinity\tGPU NUMA ID\x1b[0m\n"
+            "GPU0\t X \tNV18\t0-55\t0\t\tN/A\n"
+            "GPU1\tNV18\t X \t0-55\t0\t\tN/A\n")
+    topo = parse_topology(text)
+    assert topo == {0: {0: "X", 1: "NV18"}, 1: {0: "NV18", 1: "X"}}
+
+    class Fake:
+        stdout = text
+
+    view = nvlink_topology(0, runner=lambda *a, **k: Fake())
+    assert view == {"gpus": 2, "peers": {"1": {"link": "NV18", "nvlinks": 18}},
+                    "all_nvlink": True}
+
+
 def test_topology_parsing_with_fake_nvidia_smi():
     topo = parse_topology(TOPO)
     assert topo[0][1] == "NV18" and topo[2][0] == "NV18" and topo[1][1] == "X"
