@@ -298,8 +298,9 @@ class Gemm:
         self.name = f"gemm{size}"
         self.dtype = dtype
         self.size = size
-        self.kernel = "gemm_tc_kernel<256,dense>"
         self.params = default_params("gemm")
+        self.kernel = (f"gemm_tc2_kernel<{self.params['BLOCK_N']}>" if self.params.get("CTA_GROUP") == 2
+                       else f"gemm_tc_kernel<{self.params['BLOCK_N']},dense>")
         n_local = size // world if split else size
         if split and size % world:
             raise SystemExit("N must divide evenly across ranks")
@@ -479,13 +480,19 @@ class RmsnormGemm:
         return 2.0 * self.cpu_rows * self.k * self.n_local
 
 
+def grouped_kernel_label(params):
+    """Kernel(s) one grouped GEMM call launches with ``params``."""
+    bn = params.get("BLOCK_N", 256)
+    if params.get("CTA_GROUP", 1) == 2:
+        return f"gemm_tc2_kernel<{bn},grouped> + gemm_tc_kernel<{bn},grouped,tail>", 2
+    return f"gemm_tc_kernel<{bn},grouped>", 1
+
+
 class MoeSmall:
     name = "moe_small"
     unit = "TFLOP/s"
     bound = "hbm"
     dtype = "bf16"
-    kernel = "gemm_tc_kernel<256,grouped>"
-    launches_per_step = 1
 
     def __init__(self, device, rank, world):
         import torch
@@ -497,6 +504,7 @@ class MoeSmall:
         cfg = workloads.MOE_SMALL
         self.k, self.n = cfg["k"], cfg["n"]
         self.params = default_params("moe_grouped_gemm")
+        self.kernel, self.launches_per_step = grouped_kernel_label(self.params)
         x, w = workloads.moe_inputs(counts, self.k, self.n, "bf16", seed=rank, device=device)
         self.offsets = torch.tensor(workloads.offsets_from_counts(counts), dtype=torch.int32,
                                     device=device)
@@ -511,6 +519,10 @@ class MoeSmall:
         self.Y = [torch.empty(t, self.n, device=device, dtype=x.dtype) for _ in range(self.sets)]
         self.counts = counts
         self.sm = torch.cuda.get_device_properties(device).multi_processor_count
+
+    def dominant_kernel(self, i):
+        """The grouped GEMM call (pair + tail launches when CTA_GROUP is 2)."""
+        self.step(i)
 
     def step(self, i):
         from flashattentionanycard_b200.kernels import moe_grouped_gemm
@@ -562,8 +574,6 @@ class MoeLarge:
     unit = "TFLOP/s"
     bound = "tensor"
     dtype = "bf16"
-    kernel = "gemm_tc_kernel<256,grouped>"
-    launches_per_step = 5  # route: count, scan, scatter; gather; grouped GEMM
 
     def __init__(self, device, rank, world):
         import torch
@@ -577,6 +587,8 @@ class MoeLarge:
         self.cfg = cfg
         self.world, self.rank = world, rank
         self.params = default_params("moe_grouped_gemm")
+        self.kernel, gemm_launches = grouped_kernel_label(self.params)
+        self.launches_per_step = 4 + gemm_launches  # route: count, scan, scatter; gather; GEMM
         self.x, self.w, ids = workloads.moe_large_inputs("bf16", seed=0, device=device,
                                                          experts=cfg["experts"])
         self.sm = torch.cuda.get_device_properties(device).multi_processor_count
@@ -612,12 +624,16 @@ class MoeLarge:
             self.ep = ep.PeerExpertParallelMoE(local, self.placement, self.plan, rank, world,
                                                cfg["topk"], tpr, group=dist.group.WORLD,
                                                params=self.params, sm_count=self.sm)
-            self.launches_per_step = 7  # route x3, plan, rowmap, dispatch, grouped GEMM
+            # route x3, plan, rowmap, dispatch, grouped GEMM with the peer-scatter epilogue
+            label, gemm_launches = grouped_kernel_label(self.params)
+            self.kernel = label.replace(",grouped", ",grouped,scatter")
+            self.launches_per_step = 6 + gemm_launches
         else:
             self.ep = ep.ExpertParallelMoE(local, self.placement, self.plan, rank, world,
                                            cfg["topk"], tpr, group=dist.group.WORLD,
                                            params=self.params, sm_count=self.sm)
-            self.launches_per_step = 21  # routing/keys/sorts/checks + 4 gathers + GEMM
+            # routing/keys/sorts/checks + 4 gathers + grouped GEMM
+            self.launches_per_step = 20 + grouped_kernel_label(self.params)[1]
         import torch
 
         torch.cuda.empty_cache()

@@ -224,8 +224,6 @@ int resolve_tc_config(const bokt_params* p, bool grouped, int experts, int smem_
   if (p->split_k > 1) return fail(BOKT_ERR_UNSUPPORTED, "split_k > 1 is not implemented");
   const int cta_group = param_or(p->cta_group, 1);
   if (cta_group != 1 && cta_group != 2) return fail(BOKT_ERR_CONFIG, "cta_group must be 1 or 2");
-  if (cta_group == 2 && grouped)
-    return fail(BOKT_ERR_UNSUPPORTED, "cta_group 2 is implemented for the dense GEMM only");
   if (cta_group == 2 && bn == 64)
     return fail(BOKT_ERR_CONFIG, "cta_group 2 needs block_n 128 or 256");
   const int raster = param_or(p->raster, bokt::kRasterExpert);
@@ -235,7 +233,7 @@ int resolve_tc_config(const bokt_params* p, bool grouped, int experts, int smem_
     return fail(BOKT_ERR_CONFIG, "raster 2 applies to the grouped GEMM (dense: group_m)");
   const int stages = param_or(p->stages, cta_group == 2 ? (bn == 256 ? 6 : 8) : (bn == 256 ? 4 : 6));
   if (stages < 2 || stages > 8) return fail(BOKT_ERR_CONFIG, "stages must be in [2, 8]");
-  int smem = cta_group == 2 ? bokt::gemm_tc2_smem_bytes(bn, stages)
+  int smem = cta_group == 2 ? bokt::gemm_tc2_smem_bytes(bn, stages, grouped ? experts : 0)
                             : bokt::gemm_tc_smem_bytes(bn, stages, grouped, experts);
   if (smem > smem_optin)
     return fail(BOKT_ERR_CONFIG, "block_n=%d stages=%d needs %d bytes of shared memory (max %d)",
@@ -253,26 +251,34 @@ int resolve_tc_config(const bokt_params* p, bool grouped, int experts, int smem_
   return BOKT_OK;
 }
 
-const void* tc2_kernel(int dtype, int bn, bool rowscale = false) {
-  if (rowscale) {
-    if (dtype == BOKT_BF16)
-      return bn == 256
-                 ? reinterpret_cast<const void*>(&bokt::gemm_tc2_kernel<256, __nv_bfloat16, true>)
-                 : reinterpret_cast<const void*>(&bokt::gemm_tc2_kernel<128, __nv_bfloat16, true>);
-    return bn == 256 ? reinterpret_cast<const void*>(&bokt::gemm_tc2_kernel<256, __half, true>)
-                     : reinterpret_cast<const void*>(&bokt::gemm_tc2_kernel<128, __half, true>);
-  }
-  if (dtype == BOKT_BF16)
-    return bn == 256 ? reinterpret_cast<const void*>(&bokt::gemm_tc2_kernel<256, __nv_bfloat16>)
-                     : reinterpret_cast<const void*>(&bokt::gemm_tc2_kernel<128, __nv_bfloat16>);
-  return bn == 256 ? reinterpret_cast<const void*>(&bokt::gemm_tc2_kernel<256, __half>)
-                   : reinterpret_cast<const void*>(&bokt::gemm_tc2_kernel<128, __half>);
+template <typename T, bool ROWSCALE, bool GROUPED, bool SCATTER = false>
+const void* tc2_kernel_for(int bn) {
+  return bn == 256
+             ? reinterpret_cast<const void*>(&bokt::gemm_tc2_kernel<256, T, ROWSCALE, GROUPED, SCATTER>)
+             : reinterpret_cast<const void*>(&bokt::gemm_tc2_kernel<128, T, ROWSCALE, GROUPED, SCATTER>);
+}
+
+const void* tc2_kernel(int dtype, int bn, bool rowscale = false, bool grouped = false,
+                       bool scatter = false) {
+  const bool bf = dtype == BOKT_BF16;
+  if (scatter)
+    return bf ? tc2_kernel_for<__nv_bfloat16, false, true, true>(bn)
+              : tc2_kernel_for<__half, false, true, true>(bn);
+  if (grouped)
+    return bf ? tc2_kernel_for<__nv_bfloat16, false, true>(bn)
+              : tc2_kernel_for<__half, false, true>(bn);
+  if (rowscale)
+    return bf ? tc2_kernel_for<__nv_bfloat16, true, false>(bn)
+              : tc2_kernel_for<__half, true, false>(bn);
+  return bf ? tc2_kernel_for<__nv_bfloat16, false, false>(bn)
+            : tc2_kernel_for<__half, false, false>(bn);
 }
 
 // Dense GEMM on CTA pairs: cluster of 2 along x, PDL as every other launch.
 int launch_tc2(int dtype, const TcConfig& cfg, const CUtensorMap& ma, const CUtensorMap& mb,
-               const GemmTcArgs& args, int pairs, cudaStream_t s) {
-  const void* fn = tc2_kernel(dtype, cfg.bn, args.row_scale != nullptr);
+               const GemmTcArgs& args, int pairs, cudaStream_t s, bool grouped = false,
+               bool scatter = false) {
+  const void* fn = tc2_kernel(dtype, cfg.bn, args.row_scale != nullptr, grouped, scatter);
   int rc = ensure_smem(fn, cfg.smem);
   if (rc) return rc;
   void* kargs[] = {const_cast<CUtensorMap*>(&ma), const_cast<CUtensorMap*>(&mb),
@@ -596,6 +602,7 @@ int grouped_gemm_impl(const void* X, const void* W, const void* offsets, int off
                ? launch_simt<__nv_bfloat16>(X, W, Y, T, N, K, offsets, offsets_is_i64, E, s)
                : launch_simt<__half>(X, W, Y, T, N, K, offsets, offsets_is_i64, E, s);
   }
+  const bokt_params zero = {};
   TcConfig cfg;
   rc = resolve_tc_config(params, true, E, dev.smem_optin, &cfg);
   if (rc) return rc;
@@ -628,9 +635,35 @@ int grouped_gemm_impl(const void* X, const void* W, const void* offsets, int off
     args.rows_per_owner = scatter->rows_per_owner;
     args.owners = scatter->owners;
   }
-  const bokt_params zero = {};
   const int mult = param_or((params ? params : &zero)->cta_multiplier, 1);
   const int sms = sm_count > 0 ? sm_count : dev.sm_count;
+  const long long nn = (N + cfg.bn - 1) / cfg.bn;
+  if (cfg.cta_group == 2) {
+    // Split launch: 256-row pair tiles (every expert's rows but a <= 128-row
+    // tail) on CTA pairs, then those tails on single CTAs, which start on the
+    // SMs the pair kernel frees (see gemm_tc_kernel, kSegmentTail).
+    GemmTcArgs pa = args;
+    pa.segment = bokt::kSegmentPairs;
+    pa.idesc = bokt::make_idesc_f16(uint32_t(dtype), 256, uint32_t(cfg.bn));
+    const long long max_pair_tiles = ((long long)(T + 255) / 256 + E) * nn;
+    long long pairs = sms / 2;
+    if (pairs > max_pair_tiles) pairs = max_pair_tiles;
+    if (pairs < 1) pairs = 1;
+    rc = launch_tc2(dtype, cfg, ma, mb, pa, int(pairs), s, /*grouped=*/true, scatter != nullptr);
+    if (rc) return rc;
+    bokt_params single = params ? *params : zero;
+    single.cta_group = 1;
+    single.stages = 0;  // the single-CTA kernel's default depth for this block_n
+    TcConfig tcfg;
+    rc = resolve_tc_config(&single, true, E, dev.smem_optin, &tcfg);
+    if (rc) return rc;
+    GemmTcArgs ta = args;
+    ta.segment = bokt::kSegmentTail;
+    ta.stages = tcfg.stages;
+    long long tail_grid = (long long)E * nn;  // at most one tail tile per expert and column block
+    if (tail_grid > sms) tail_grid = sms;
+    return launch_tc(true, dtype, tcfg, ma, mb, ta, int(tail_grid), s, scatter != nullptr);
+  }
   // Upper bound on tiles without reading offsets: sum_e cdiv(c_e, 128) <= cdiv(T, 128) + E.
   const long long max_tiles = ((long long)(T + 127) / 128 + E) * ((N + cfg.bn - 1) / cfg.bn);
   long long grid = (long long)sms * mult;
@@ -1031,7 +1064,7 @@ int bokt_kernel_attrs(int kernel, int dtype, int n, int k, const bokt_params* pa
       TcConfig cfg;
       rc = resolve_tc_config(params, grouped, grouped ? 64 : 0, dev.smem_optin, &cfg);
       if (rc) return rc;
-      fn = cfg.cta_group == 2 ? tc2_kernel(dtype, cfg.bn, norm)
+      fn = cfg.cta_group == 2 ? tc2_kernel(dtype, cfg.bn, norm, grouped)
                               : tc_kernel(grouped, dtype, cfg.bn, false, norm);
       dyn = cfg.smem;
       threads = bokt::kGemmThreads;

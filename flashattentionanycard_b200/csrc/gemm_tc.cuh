@@ -49,12 +49,19 @@ struct GemmTcArgs {
   // epilogue before rounding (the RMSNorm row factor of the fused
   // RMSNorm -> GEMM, whose norm weight is folded into B).
   const float* row_scale;
+  // Grouped GEMM split across two launches (CTA pairs + single CTAs): which
+  // rows of each expert this launch covers (kSegmentAll / kSegmentPairs /
+  // kSegmentTail, see expert_rows).
+  int segment;
   // Grouped tile order: kRasterExpert walks experts in index order (M fastest
   // inside an expert); kRasterBalanced spreads the tiles of low-reuse experts
   // (at most kLowReuseMBlocks row blocks) evenly between the others.
   int raster;
 };
 
+constexpr int kSegmentAll = 0;    // every row (one launch)
+constexpr int kSegmentPairs = 1;  // rows in 256-row pair tiles (see expert_rows)
+constexpr int kSegmentTail = 2;   // the <= 128-row tail left to single CTAs
 constexpr int kRasterExpert = 1;
 constexpr int kRasterBalanced = 2;
 constexpr int kLowReuseMBlocks = 2;
@@ -168,6 +175,12 @@ struct GroupedSchedule {
   int* totals;   // [3]   all tiles, low-reuse tiles, high-reuse entries
 };
 
+// Rows [start, start + count) of expert e covered by this launch.  Split
+// launches: an expert of c rows has c mod 256 = t tail rows; the pair launch
+// takes all rows when t == 0 or t > 128 (the last pair tile is padded, as two
+// 128-row tiles would be) and all but the tail when 0 < t <= 128; the
+// single-CTA launch takes exactly that tail.  Together they cover each row
+// once, with the same padding as 128-row tiles alone.
 __device__ __forceinline__ void expert_rows(const GemmTcArgs& args, int e, int* start, int* count) {
   long long s, t;
   if (args.offsets_i64) {
@@ -180,14 +193,27 @@ __device__ __forceinline__ void expert_rows(const GemmTcArgs& args, int e, int* 
   const long long T = args.M;
   s = s < 0 ? 0 : (s > T ? T : s);
   t = t < s ? s : (t > T ? T : t);
-  *start = static_cast<int>(s);
-  *count = static_cast<int>(t - s);
+  int st = static_cast<int>(s);
+  int c = static_cast<int>(t - s);
+  if (args.segment != kSegmentAll) {
+    const int tail = c % (2 * kGemmBM);
+    const bool short_tail = tail > 0 && tail <= kGemmBM;
+    if (args.segment == kSegmentPairs) {
+      c -= short_tail ? tail : 0;
+    } else {
+      st += c - (short_tail ? tail : 0);
+      c = short_tail ? tail : 0;
+    }
+  }
+  *start = st;
+  *count = c;
 }
 
 // Build the schedule with every thread of the CTA.  `scratch` holds 4 ints per
 // thread.  Ends with the schedule complete but without a barrier after it.
 __device__ __forceinline__ void build_grouped_schedule(const GemmTcArgs& args, int nn,
-                                                       const GroupedSchedule& g, int* scratch) {
+                                                       const GroupedSchedule& g, int* scratch,
+                                                       int tile_rows = kGemmBM) {
   const int E = args.E;
   const int nt = blockDim.x;
   const int per = (E + nt - 1) / nt;
@@ -198,7 +224,7 @@ __device__ __forceinline__ void build_grouped_schedule(const GemmTcArgs& args, i
   for (int e = e0; e < e1; ++e) {
     int st, c;
     expert_rows(args, e, &st, &c);
-    const int mb = (c + kGemmBM - 1) / kGemmBM;
+    const int mb = (c + tile_rows - 1) / tile_rows;
     if (balanced && mb <= kLowReuseMBlocks) {
       ++le;
       lt += mb * nn;
@@ -236,7 +262,7 @@ __device__ __forceinline__ void build_grouped_schedule(const GemmTcArgs& args, i
   for (int e = e0; e < e1; ++e) {
     int st, c;
     expert_rows(args, e, &st, &c);
-    const int mb = (c + kGemmBM - 1) / kGemmBM;
+    const int mb = (c + tile_rows - 1) / tile_rows;
     int pos;
     if (balanced && mb <= kLowReuseMBlocks) {
       pos = lpos++;
@@ -254,7 +280,8 @@ __device__ __forceinline__ void build_grouped_schedule(const GemmTcArgs& args, i
 }
 
 __device__ __forceinline__ TileCoord grouped_tile(int t, const GroupedSchedule& g, int E, int nn,
-                                                  int bn, int raster, bool* low) {
+                                                  int bn, int raster, bool* low,
+                                                  int tile_rows = kGemmBM) {
   const int total = g.totals[0];
   const int nlow = g.totals[1];
   int u = t;
@@ -276,17 +303,17 @@ __device__ __forceinline__ TileCoord grouped_tile(int t, const GroupedSchedule& 
   }
   const int rel = u - g.pre[lo];
   const int count = g.pcount[lo];
-  const int mblocks = (count + kGemmBM - 1) / kGemmBM;
+  const int mblocks = (count + tile_rows - 1) / tile_rows;
   // M fastest inside an expert: all row blocks of one weight column block run
   // together, so W[e][:, n-block] is fetched from HBM once and reused from L2.
   const int mb = rel % mblocks;
   const int nb = rel / mblocks;
   TileCoord c;
-  c.a_row = g.pstart[lo] + mb * kGemmBM;
+  c.a_row = g.pstart[lo] + mb * tile_rows;
   c.n0 = nb * bn;
   c.expert = g.pexp[lo];
   c.c_row = c.a_row;
-  c.rows_valid = min(kGemmBM, count - mb * kGemmBM);
+  c.rows_valid = min(tile_rows, count - mb * tile_rows);
   *low = lo >= g.totals[2];
   return c;
 }
@@ -344,8 +371,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tmem_relinquish();
   }
   // Prologue above overlaps the previous kernel; global memory only after this.
+  // Exception: the single-CTA tail of a split grouped launch is launched right
+  // behind the pair kernel, which releases it only after the pair kernel's own
+  // predecessor has completed; the tail reads nothing the pair kernel writes
+  // and writes other rows, so it starts at once (filling the SMs the pair
+  // kernel frees) and waits for the pair kernel only before it exits, so that
+  // whatever follows the tail sees both launches complete.
+  const bool tail_behind_pairs = GROUPED && args.segment == kSegmentTail;
   pdl_allow_next();
-  pdl_wait();
+  if (!tail_behind_pairs) pdl_wait();
 
   int ntiles;
   if constexpr (GROUPED) {
@@ -505,6 +539,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, Shape::kTmemCols);
   }
+  if (tail_behind_pairs) pdl_wait();
 }
 
 }  // namespace bokt

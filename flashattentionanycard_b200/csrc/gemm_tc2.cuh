@@ -30,14 +30,22 @@ struct GemmTc2Shape {
   static_assert(BN == 128 || BN == 256, "pair tiles need BN of 128 or 256");
 };
 
-__host__ __device__ inline int gemm_tc2_smem_bytes(int bn, int stages) {
+__host__ __device__ inline int gemm_tc2_smem_bytes(int bn, int stages, int experts = 0) {
   return 1024 + stages * (kGemmABytes + (bn / 2) * kGemmBK * 2) + kEpiBytes +
-         (2 * stages + 4) * 8 + 16;
+         (2 * stages + 4) * 8 + 16 + (experts > 0 ? (4 * experts + 4) * 4 : 0);
 }
 
 // ROWSCALE: the epilogue scales C row m by args.row_scale[m] (fp32) before
 // rounding (fused RMSNorm -> GEMM with the norm weight folded into B).
-template <int BN, typename OutT, bool ROWSCALE = false>
+// GROUPED: the MoE grouped GEMM on 256-row pair tiles inside each expert
+// (kernels/moe_grouped_gemm.py:11-58; schedule built per CTA from the device
+// offsets, W read through a 3-D tensor map [E][K][N]).  With
+// args.segment == kSegmentPairs it covers the pair part of a split launch and
+// releases the dependent launch (the single-CTA tail) only after its own
+// predecessor has completed.
+// SCATTER (grouped only): the expert-parallel epilogue of gemm_tc_kernel —
+// packed row l goes to its token owner's buffer (possibly a peer GPU's).
+template <int BN, typename OutT, bool ROWSCALE = false, bool GROUPED = false, bool SCATTER = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     GemmTcArgs args) {
@@ -56,6 +64,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  GroupedSchedule sched;  // GROUPED only: [E+1] + 3 x [E] + [3] ints
+  sched.pre = reinterpret_cast<int*>(tmem_holder + 4);
+  sched.pstart = sched.pre + (args.E + 1);
+  sched.pcount = sched.pstart + args.E;
+  sched.pexp = sched.pcount + args.E;
+  sched.totals = sched.pexp + args.E;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -66,7 +80,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int M = args.M, N = args.N;
   const int nm = (M + 2 * kGemmBM - 1) / (2 * kGemmBM);
   const int nn = (N + BN - 1) / BN;
-  const int ntiles = nm * nn;
   const int nkb = (args.K + kGemmBK - 1) / kGemmBK;
 
   if (threadIdx.x == 0) {
@@ -89,22 +102,42 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tmem_alloc_pair(tmem_holder, Shape::kTmemCols);
     tmem_relinquish_pair();
   }
-  pdl_allow_next();
-  pdl_wait();
+  if constexpr (GROUPED) {
+    pdl_wait();
+    pdl_allow_next();
+    // Every CTA builds the same schedule; the epilogue staging area is free
+    // until the first tile and serves as scan scratch.
+    build_grouped_schedule(args, nn, sched, reinterpret_cast<int*>(sEpi), 2 * kGemmBM);
+  } else {
+    pdl_allow_next();
+    pdl_wait();
+  }
   tc_fence_before();
-  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
+  cluster_sync();  // both CTAs' barriers initialised, TMEM allocated, schedule built
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  const int ntiles = GROUPED ? sched.totals[0] : nm * nn;
 
-  // 256-row tiles, GROUP_M raster as kernels/gemm.py:20-26.
-  auto tile_at = [&](int t, int& m0, int& n0) {
-    const int per_group = args.group_m * nn;
-    const int group = t / per_group;
-    const int first_m = group * args.group_m;
-    const int gm = min(nm - first_m, args.group_m);
-    const int local = t - group * per_group;
-    m0 = (first_m + local % gm) * 2 * kGemmBM;
-    n0 = (local / gm) * BN;
+  // 256-row tiles: dense in the GROUP_M raster of kernels/gemm.py:20-26;
+  // grouped inside each expert (rows_valid = rows of the expert in the tile).
+  auto tile_at = [&](int t) -> TileCoord {
+    if constexpr (GROUPED) {
+      bool low;
+      return grouped_tile(t, sched, args.E, nn, BN, args.raster, &low, 2 * kGemmBM);
+    } else {
+      const int per_group = args.group_m * nn;
+      const int group = t / per_group;
+      const int first_m = group * args.group_m;
+      const int gm = min(nm - first_m, args.group_m);
+      const int local = t - group * per_group;
+      TileCoord c;
+      c.a_row = (first_m + local % gm) * 2 * kGemmBM;
+      c.n0 = (local / gm) * BN;
+      c.expert = 0;
+      c.c_row = c.a_row;
+      c.rows_valid = min(2 * kGemmBM, M - c.a_row);
+      return c;
+    }
   };
 
   if (warp == 0) {
@@ -114,8 +147,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int t = pair; t < ntiles && ok; t += npairs) {
-        int m0, n0;
-        tile_at(t, m0, n0);
+        const TileCoord tc = tile_at(t);
         for (int kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, abort_flag, 11)) {
             ok = false;
@@ -124,11 +156,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint32_t full_leader = map_shared(smem_addr(&full[stage]), 0);
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * Shape::kStageBytes);
           tma_load_2d_pair(sA + stage * kGemmABytes, &tmA, full_leader, kb * kGemmBK,
-                           m0 + static_cast<int>(rank) * kGemmBM);
+                           tc.a_row + static_cast<int>(rank) * kGemmBM);
 #pragma unroll
-          for (int c = 0; c < Shape::kBHalf / 64; ++c)
-            tma_load_2d_pair(sB + stage * Shape::kBBytes + c * 8192, &tmB, full_leader,
-                             n0 + static_cast<int>(rank) * Shape::kBHalf + c * 64, kb * kGemmBK);
+          for (int c = 0; c < Shape::kBHalf / 64; ++c) {
+            const int col = tc.n0 + static_cast<int>(rank) * Shape::kBHalf + c * 64;
+            if constexpr (GROUPED) {
+              tma_load_3d_pair(sB + stage * Shape::kBBytes + c * 8192, &tmB, full_leader, col,
+                               kb * kGemmBK, tc.expert);
+            } else {
+              tma_load_2d_pair(sB + stage * Shape::kBBytes + c * 8192, &tmB, full_leader, col,
+                               kb * kGemmBK);
+            }
+          }
           if (++stage == stages) {
             stage = 0;
             phase ^= 1u;
@@ -183,8 +222,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     OutT** rowptr = reinterpret_cast<OutT**>(sEpi + kEpiWarps * kEpiStageBytes) + (warp - 2) * 32;
     int i = 0;
     for (int t = pair; t < ntiles; t += npairs, ++i) {
-      int m0, n0;
-      tile_at(t, m0, n0);
+      const TileCoord tc = tile_at(t);
       const int acc = i & 1;
       const uint32_t acc_phase = (static_cast<uint32_t>(i) >> 1) & 1u;
       const bool ok = mbar_wait_cluster(&tfull[acc], acc_phase, abort_flag, 14);
@@ -192,16 +230,34 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      const int row = m0 + static_cast<int>(rank) * kGemmBM + r;
-      rowptr[lane] = row < M ? C + static_cast<size_t>(row) * N + n0 : nullptr;
+      // This CTA's accumulator rows are tile rows [128 rank, 128 rank + 128).
+      const int local = static_cast<int>(rank) * kGemmBM + r;
+      bool row_ok = local < tc.rows_valid;
+      const int row = tc.c_row + local;
+      OutT* crow = row_ok ? C + static_cast<size_t>(row) * N + tc.n0 : nullptr;
+      if constexpr (SCATTER) {
+        if (row_ok) {
+          const int a = args.rowmap[row];
+          const int o = a / args.rows_per_owner;
+          if (a < 0 || o >= args.owners) {
+            report_status(kStatusBadExpertId, row);
+            crow = nullptr;
+          } else {
+            crow = reinterpret_cast<OutT*>(args.out_ptrs[o]) +
+                   static_cast<size_t>(a - o * args.rows_per_owner) * N + tc.n0;
+          }
+        }
+      }
+      rowptr[lane] = crow;
       float scale = 1.f;
-      if constexpr (ROWSCALE) scale = row < M ? args.row_scale[row] : 1.f;
+      if constexpr (ROWSCALE) scale = row_ok ? args.row_scale[row] : 1.f;
       __syncwarp();
-      epilogue_store_tile<BN, OutT, ROWSCALE>(taddr, stage, rowptr, n0, N, lane, scale);
+      epilogue_store_tile<BN, OutT, ROWSCALE>(taddr, stage, rowptr, tc.n0, N, lane, scale);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(map_shared(smem_addr(&tempty[acc]), 0));
     }
+    if constexpr (SCATTER) __threadfence_system();  // peer stores visible before the barrier
   }
 
   // ---------------------------------------------------------------- teardown

@@ -121,10 +121,11 @@ def gemm_shared_bytes(block_n, stages, experts=0):
     return total
 
 
-def gemm_pair_shared_bytes(block_n, stages):
+def gemm_pair_shared_bytes(block_n, stages, experts=0):
     """Dynamic shared memory per CTA of the CTA-pair GEMM (csrc/gemm_tc2.cuh)."""
     return (1024 + stages * (GEMM_BM * GEMM_BK * 2 + (block_n // 2) * GEMM_BK * 2)
-            + EPILOGUE_BYTES + (2 * stages + 4) * 8 + 16)
+            + EPILOGUE_BYTES + (2 * stages + 4) * 8 + 16
+            + ((4 * experts + 4) * 4 if experts else 0))
 
 
 def rmsnorm_ring_bytes(columns, stages, elem_bytes=2):
@@ -178,10 +179,10 @@ def prune_reason(hardware, kernel, params, columns=0, heuristic_smem=False):
     if params["BLOCK_N"] not in (64, 128, 256) or 2 * params["BLOCK_N"] > TMEM_COLUMNS:
         return "illegal_tile_shape"
     pair = params.get("CTA_GROUP", 1) == 2
-    if pair and (kernel != "gemm" or params["BLOCK_N"] == 64):
+    if pair and params["BLOCK_N"] == 64:
         return "illegal_tile_shape"
     experts = 64 if kernel == "moe_grouped_gemm" else 0
-    smem = (gemm_pair_shared_bytes(params["BLOCK_N"], params["num_stages"]) if pair
+    smem = (gemm_pair_shared_bytes(params["BLOCK_N"], params["num_stages"], experts) if pair
             else gemm_shared_bytes(params["BLOCK_N"], params["num_stages"], experts))
     if smem > hardware.shared_memory_per_block:
         return "shared_memory_exceeds_device_limit"

@@ -166,6 +166,45 @@ def test_grouped_gemm_balanced_raster_many_experts(experts, cuda_device):
     assert torch.equal(outs[0], outs[1])
 
 
+@pytest.mark.parametrize("params", [{"BLOCK_N": 256, "num_stages": 6, "CTA_GROUP": 2},
+                                    {"BLOCK_N": 128, "num_stages": 8, "CTA_GROUP": 2},
+                                    {"BLOCK_N": 256, "num_stages": 4, "CTA_GROUP": 2,
+                                     "RASTER": 2}])
+def test_grouped_gemm_pair_split_covers_every_row(params, cuda_device):
+    """CTA_GROUP 2: pair tiles take each expert's rows but a <= 128-row tail,
+    a single-CTA launch takes the tails.  Expert sizes around every multiple of
+    128 and 256; every row of the NaN-prefilled output is written exactly as
+    the oracle says, and rows before offsets[0] / after offsets[E] stay NaN."""
+    n, k = 392, 200
+    sizes = [0, 1, 127, 128, 129, 255, 256, 257, 383, 384, 385, 511, 512, 513, 700, 1000]
+    rng = np.random.default_rng(1)
+    counts = sizes + rng.integers(0, 600, size=20).tolist()
+    lead, trail = 3, 5
+    starts = [lead]
+    for c in counts:
+        starts.append(starts[-1] + c)
+    rows = starts[-1] + trail
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(rows, k, generator=g).bfloat16()
+    w = (0.5 * torch.randn(len(counts), k, n, generator=g)).bfloat16()
+    ref = numerics.grouped_gemm_fp32(as_f32(x), as_f32(w), starts)
+    out = nan_like((rows, n), "bf16", cuda_device)
+    offsets = torch.tensor(starts, dtype=torch.int64, device=cuda_device)
+    compiled = moe_grouped_gemm.launch(x.to(cuda_device), w.to(cuda_device), offsets, out,
+                                       params, 148)
+    torch.cuda.synchronize()
+    assert compiled.path == "tcgen05" and compiled.n_spills == 0
+    got = out.float().cpu().numpy()
+    assert np.isnan(got[:lead]).all() and np.isnan(got[rows - trail:]).all()
+    gate(out[lead:rows - trail], ref[lead:rows - trail], "bf16")
+    single = nan_like((rows, n), "bf16", cuda_device)
+    moe_grouped_gemm.launch(x.to(cuda_device), w.to(cuda_device), offsets, single,
+                            dict(params, CTA_GROUP=1, num_stages=4), 148)
+    torch.cuda.synchronize()
+    diff = (single[lead:rows - trail].float() - out[lead:rows - trail].float()).abs().max().item()
+    assert diff <= 0.05 * float(np.nanmax(np.abs(ref)))
+
+
 def test_grouped_gemm_leaves_rows_outside_experts(cuda_device):
     """Rows before offsets[0] and after offsets[E] are not written (reference
     kernel writes only [start, start + count) per expert)."""

@@ -51,12 +51,12 @@ def test_every_full_space_config_is_classified(hardware):
         legal = [p for p in grid_configs(search_space(kernel)) if prune_reason(hardware, kernel, p) is None]
         assert legal, kernel
         for p in legal:
+            experts = 64 if kernel == "moe_grouped_gemm" else 0
             if p.get("CTA_GROUP", 1) == 2:
-                assert gemm_pair_shared_bytes(p["BLOCK_N"], p["num_stages"]) <= 227 * 1024
+                assert gemm_pair_shared_bytes(p["BLOCK_N"], p["num_stages"], experts) <= 227 * 1024
             else:
                 assert gemm_shared_bytes(p["BLOCK_N"], p["num_stages"], 64) <= 227 * 1024
-        if kernel == "gemm":
-            assert any(p["CTA_GROUP"] == 2 for p in legal)
+        assert any(p["CTA_GROUP"] == 2 for p in legal)
 
 
 def test_rmsnorm_limit(hardware):
