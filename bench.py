@@ -481,10 +481,10 @@ class RmsnormGemm:
 
 
 def grouped_kernel_label(params):
-    """Kernel(s) one grouped GEMM call launches with ``params``."""
+    """(kernel, launches) of one grouped GEMM call with ``params``."""
     bn = params.get("BLOCK_N", 256)
     if params.get("CTA_GROUP", 1) == 2:
-        return f"gemm_tc2_kernel<{bn},grouped> + gemm_tc_kernel<{bn},grouped,tail>", 2
+        return f"gemm_tc2_kernel<{bn},grouped>", 1
     return f"gemm_tc_kernel<{bn},grouped>", 1
 
 
@@ -504,8 +504,7 @@ class MoeSmall:
         cfg = workloads.MOE_SMALL
         self.k, self.n = cfg["k"], cfg["n"]
         # Tuned for this single-wave problem (120 tiles of 128 rows on 148 SMs):
-        # one launch of single-CTA tiles; CTA pairs plus a tail launch measured
-        # 21.5 us against 12.5 us.
+        # single-CTA tiles.
         self.params = dict(default_params("moe_grouped_gemm"), CTA_GROUP=1, num_stages=4)
         self.kernel, self.launches_per_step = grouped_kernel_label(self.params)
         x, w = workloads.moe_inputs(counts, self.k, self.n, "bf16", seed=rank, device=device)

@@ -13,9 +13,9 @@ kernels:
   grouped-M raster of the dense GEMM; ``CTA_MULTIPLIER`` the persistent grid
   of the grouped GEMM (``sm_count * CTA_MULTIPLIER``).
 * ``CTA_GROUP`` 1 (one CTA per 128-row tile) or 2 (CTA pairs on two SMs,
-  tcgen05 cta_group::2, 256-row tiles).  For the MoE grouped GEMM, 2 runs each
-  expert's rows on pair tiles except a tail of at most 128 rows, which a
-  single-CTA launch behind it computes (same padding as 128-row tiles).
+  tcgen05 cta_group::2, 256-row tiles).  For the MoE grouped GEMM, 2 cuts each
+  expert into 256-row pair tiles and a last block of at most 128 rows as a
+  half-height pair tile (M = 128), so padding stays that of 128-row tiles.
 * MoE grouped GEMM only: ``RASTER`` 1 walks the tiles expert by expert; 2 spreads
   the tiles of experts with at most two 128-row blocks (weights read once or
   twice: HBM-bound) evenly between the tiles of the others (tensor-bound).
@@ -117,7 +117,7 @@ def default_params(kernel: str) -> dict[str, int]:
     if kernel == "gemm":
         p.update(GROUP_M=8, CTA_GROUP=2, num_stages=6)
     else:
-        # CTA pairs (tails on single CTAs): 1,171 vs 914 TFLOP/s at 64 experts.
+        # CTA pairs (half-height tiles for short tails): 1,194 vs 975 TFLOP/s at 64 experts.
         p.update(CTA_MULTIPLIER=1, RASTER=1, CTA_GROUP=2, num_stages=6)
     return p
 

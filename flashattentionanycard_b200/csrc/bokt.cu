@@ -277,12 +277,13 @@ const void* tc2_kernel(int dtype, int bn, bool rowscale = false, bool grouped = 
 // Dense GEMM on CTA pairs: cluster of 2 along x, PDL as every other launch.
 int launch_tc2(int dtype, const TcConfig& cfg, const CUtensorMap& ma, const CUtensorMap& mb,
                const GemmTcArgs& args, int pairs, cudaStream_t s, bool grouped = false,
-               bool scatter = false) {
+               bool scatter = false, const CUtensorMap* ma64 = nullptr) {
   const void* fn = tc2_kernel(dtype, cfg.bn, args.row_scale != nullptr, grouped, scatter);
   int rc = ensure_smem(fn, cfg.smem);
   if (rc) return rc;
+  // Third map: 64-row A boxes for grouped half-height tiles (unused by dense launches).
   void* kargs[] = {const_cast<CUtensorMap*>(&ma), const_cast<CUtensorMap*>(&mb),
-                   const_cast<GemmTcArgs*>(&args)};
+                   const_cast<CUtensorMap*>(ma64 ? ma64 : &ma), const_cast<GemmTcArgs*>(&args)};
   cudaLaunchAttribute attr[2];
   cudaLaunchConfig_t lc = launch_config(
       dim3(2 * pairs), dim3(bokt::kGemmThreads), cfg.smem, s,
@@ -639,33 +640,24 @@ int grouped_gemm_impl(const void* X, const void* W, const void* offsets, int off
   const int sms = sm_count > 0 ? sm_count : dev.sm_count;
   const long long nn = (N + cfg.bn - 1) / cfg.bn;
   if (cfg.cta_group == 2) {
-    // Split launch: 256-row pair tiles (every expert's rows but a <= 128-row
-    // tail) on CTA pairs, then those tails on single CTAs, which start on the
-    // SMs the pair kernel frees (see gemm_tc_kernel, kSegmentTail).
+    // CTA pairs: 256-row tiles per expert, a last block of <= 128 rows as a
+    // half-height tile (M = 128, 64 rows per CTA, A boxes of 64 rows).
+    CUtensorMap ma64;
+    const uint32_t ba64[2] = {64, 64};
+    rc = encode_map(&ma64, X, 2, da, sa, ba64, dtype == BOKT_FP16);
+    if (rc) return rc;
     GemmTcArgs pa = args;
-    pa.segment = bokt::kSegmentPairs;
     pa.idesc = bokt::make_idesc_f16(uint32_t(dtype), 256, uint32_t(cfg.bn));
+    pa.idesc_half = bokt::make_idesc_f16(uint32_t(dtype), 128, uint32_t(cfg.bn));
     const long long max_pair_tiles = ((long long)(T + 255) / 256 + E) * nn;
     long long pairs = sms / 2;
     if (pairs > max_pair_tiles) pairs = max_pair_tiles;
     if (pairs < 1) pairs = 1;
-    rc = launch_tc2(dtype, cfg, ma, mb, pa, int(pairs), s, /*grouped=*/true, scatter != nullptr);
-    if (rc) return rc;
-    bokt_params single = params ? *params : zero;
-    single.cta_group = 1;
-    single.stages = 0;  // the single-CTA kernel's default depth for this block_n
-    TcConfig tcfg;
-    rc = resolve_tc_config(&single, true, E, dev.smem_optin, &tcfg);
-    if (rc) return rc;
-    GemmTcArgs ta = args;
-    ta.segment = bokt::kSegmentTail;
-    ta.stages = tcfg.stages;
-    long long tail_grid = (long long)E * nn;  // at most one tail tile per expert and column block
-    if (tail_grid > sms) tail_grid = sms;
-    return launch_tc(true, dtype, tcfg, ma, mb, ta, int(tail_grid), s, scatter != nullptr);
+    return launch_tc2(dtype, cfg, ma, mb, pa, int(pairs), s, /*grouped=*/true, scatter != nullptr,
+                      &ma64);
   }
   // Upper bound on tiles without reading offsets: sum_e cdiv(c_e, 128) <= cdiv(T, 128) + E.
-  const long long max_tiles = ((long long)(T + 127) / 128 + E) * ((N + cfg.bn - 1) / cfg.bn);
+  const long long max_tiles = ((long long)(T + 127) / 128 + E) * nn;
   long long grid = (long long)sms * mult;
   if (grid > max_tiles) grid = max_tiles;
   if (grid < 1) grid = 1;

@@ -35,6 +35,7 @@ struct GemmTcArgs {
   int group_m;  // dense raster width (tiles of M per group)
   int stages;
   uint32_t idesc;
+  uint32_t idesc_half;  // grouped CTA pairs: M = 128 (64 rows per CTA) for short tails
   const void* offsets;  // grouped only: E+1 offsets
   int offsets_i64;
   int E;
@@ -49,19 +50,12 @@ struct GemmTcArgs {
   // epilogue before rounding (the RMSNorm row factor of the fused
   // RMSNorm -> GEMM, whose norm weight is folded into B).
   const float* row_scale;
-  // Grouped GEMM split across two launches (CTA pairs + single CTAs): which
-  // rows of each expert this launch covers (kSegmentAll / kSegmentPairs /
-  // kSegmentTail, see expert_rows).
-  int segment;
   // Grouped tile order: kRasterExpert walks experts in index order (M fastest
   // inside an expert); kRasterBalanced spreads the tiles of low-reuse experts
   // (at most kLowReuseMBlocks row blocks) evenly between the others.
   int raster;
 };
 
-constexpr int kSegmentAll = 0;    // every row (one launch)
-constexpr int kSegmentPairs = 1;  // rows in 256-row pair tiles (see expert_rows)
-constexpr int kSegmentTail = 2;   // the <= 128-row tail left to single CTAs
 constexpr int kRasterExpert = 1;
 constexpr int kRasterBalanced = 2;
 constexpr int kLowReuseMBlocks = 2;
@@ -175,12 +169,7 @@ struct GroupedSchedule {
   int* totals;   // [3]   all tiles, low-reuse tiles, high-reuse entries
 };
 
-// Rows [start, start + count) of expert e covered by this launch.  Split
-// launches: an expert of c rows has c mod 256 = t tail rows; the pair launch
-// takes all rows when t == 0 or t > 128 (the last pair tile is padded, as two
-// 128-row tiles would be) and all but the tail when 0 < t <= 128; the
-// single-CTA launch takes exactly that tail.  Together they cover each row
-// once, with the same padding as 128-row tiles alone.
+// Rows [start, start + count) of expert e (offsets clamped to [0, T]).
 __device__ __forceinline__ void expert_rows(const GemmTcArgs& args, int e, int* start, int* count) {
   long long s, t;
   if (args.offsets_i64) {
@@ -193,31 +182,34 @@ __device__ __forceinline__ void expert_rows(const GemmTcArgs& args, int e, int* 
   const long long T = args.M;
   s = s < 0 ? 0 : (s > T ? T : s);
   t = t < s ? s : (t > T ? T : t);
-  int st = static_cast<int>(s);
-  int c = static_cast<int>(t - s);
-  if (args.segment != kSegmentAll) {
-    const int tail = c % (2 * kGemmBM);
-    const bool short_tail = tail > 0 && tail <= kGemmBM;
-    if (args.segment == kSegmentPairs) {
-      c -= short_tail ? tail : 0;
-    } else {
-      st += c - (short_tail ? tail : 0);
-      c = short_tail ? tail : 0;
-    }
-  }
-  *start = st;
-  *count = c;
+  *start = static_cast<int>(s);
+  *count = static_cast<int>(t - s);
 }
 
-// Build the schedule with every thread of the CTA.  `scratch` holds 4 ints per
-// thread.  Ends with the schedule complete but without a barrier after it.
+// Exclusive warp scan (lanes in order) of v; *total = sum over the warp.
+__device__ __forceinline__ int warp_exclusive_scan(int v, int lane, int* total) {
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  *total = __shfl_sync(0xffffffffu, x, 31);
+  return x - v;
+}
+
+// Build the schedule with warp 0 of the CTA (lane i owns a contiguous run of
+// experts, one warp-shuffle scan per count; no block barrier inside: the
+// caller's barrier publishes the schedule).  `warp0` selects the building
+// warp; other threads return at once.
 __device__ __forceinline__ void build_grouped_schedule(const GemmTcArgs& args, int nn,
-                                                       const GroupedSchedule& g, int* scratch,
+                                                       const GroupedSchedule& g, bool warp0,
                                                        int tile_rows = kGemmBM) {
+  if (!warp0) return;
+  const int lane = threadIdx.x & 31;
   const int E = args.E;
-  const int nt = blockDim.x;
-  const int per = (E + nt - 1) / nt;
-  const int e0 = min(E, static_cast<int>(threadIdx.x) * per);
+  const int per = (E + 31) / 32;
+  const int e0 = min(E, lane * per);
   const int e1 = min(E, e0 + per);
   const bool balanced = args.raster == kRasterBalanced;
   int he = 0, le = 0, ht = 0, lt = 0;
@@ -233,32 +225,17 @@ __device__ __forceinline__ void build_grouped_schedule(const GemmTcArgs& args, i
       ht += mb * nn;
     }
   }
-  int* mine = scratch + 4 * threadIdx.x;
-  mine[0] = he;
-  mine[1] = le;
-  mine[2] = ht;
-  mine[3] = lt;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int acc[4] = {0, 0, 0, 0};
-    for (int i = 0; i < nt; ++i) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int v = scratch[4 * i + j];
-        scratch[4 * i + j] = acc[j];
-        acc[j] += v;
-      }
-    }
-    g.totals[0] = acc[2] + acc[3];
-    g.totals[1] = acc[3];
-    g.totals[2] = acc[0];
-    g.pre[E] = acc[2] + acc[3];
+  int n_he, n_le, n_ht, n_lt;
+  int hpos = warp_exclusive_scan(he, lane, &n_he);
+  int lpos = warp_exclusive_scan(le, lane, &n_le) + n_he;
+  int htile = warp_exclusive_scan(ht, lane, &n_ht);
+  int ltile = warp_exclusive_scan(lt, lane, &n_lt) + n_ht;
+  if (lane == 0) {
+    g.totals[0] = n_ht + n_lt;
+    g.totals[1] = n_lt;
+    g.totals[2] = n_he;
+    g.pre[E] = n_ht + n_lt;
   }
-  __syncthreads();
-  int hpos = mine[0];
-  int lpos = g.totals[2] + mine[1];
-  int htile = mine[2];
-  int ltile = (g.totals[0] - g.totals[1]) + mine[3];
   for (int e = e0; e < e1; ++e) {
     int st, c;
     expert_rows(args, e, &st, &c);
@@ -371,20 +348,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tmem_relinquish();
   }
   // Prologue above overlaps the previous kernel; global memory only after this.
-  // Exception: the single-CTA tail of a split grouped launch is launched right
-  // behind the pair kernel, which releases it only after the pair kernel's own
-  // predecessor has completed; the tail reads nothing the pair kernel writes
-  // and writes other rows, so it starts at once (filling the SMs the pair
-  // kernel frees) and waits for the pair kernel only before it exits, so that
-  // whatever follows the tail sees both launches complete.
-  const bool tail_behind_pairs = GROUPED && args.segment == kSegmentTail;
   pdl_allow_next();
-  if (!tail_behind_pairs) pdl_wait();
+  pdl_wait();
 
   int ntiles;
   if constexpr (GROUPED) {
-    // The epilogue staging area is free until the first tile: scratch for the scan.
-    build_grouped_schedule(args, nn, sched, reinterpret_cast<int*>(sEpi));
+    build_grouped_schedule(args, nn, sched, threadIdx.x < 32);
   }
   tc_fence_before();
   __syncthreads();
@@ -539,7 +508,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, Shape::kTmemCols);
   }
-  if (tail_behind_pairs) pdl_wait();
 }
 
 }  // namespace bokt

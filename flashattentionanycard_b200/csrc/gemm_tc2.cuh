@@ -37,18 +37,22 @@ __host__ __device__ inline int gemm_tc2_smem_bytes(int bn, int stages, int exper
 
 // ROWSCALE: the epilogue scales C row m by args.row_scale[m] (fp32) before
 // rounding (fused RMSNorm -> GEMM with the norm weight folded into B).
-// GROUPED: the MoE grouped GEMM on 256-row pair tiles inside each expert
+// GROUPED: the MoE grouped GEMM on pair tiles inside each expert
 // (kernels/moe_grouped_gemm.py:11-58; schedule built per CTA from the device
-// offsets, W read through a 3-D tensor map [E][K][N]).  With
-// args.segment == kSegmentPairs it covers the pair part of a split launch and
-// releases the dependent launch (the single-CTA tail) only after its own
-// predecessor has completed.
+// offsets, W read through a 3-D tensor map [E][K][N]).  An expert's rows are
+// cut into 256-row tiles (M = 256, 128 rows per CTA); a last block of at most
+// 128 rows is a half-height tile (tcgen05 M = 128, 64 rows per CTA, A box of
+// 64 rows from tmA64), so padding stays that of 128-row tiles and the weight
+// column block of a short tail is read alongside the expert's other tiles.
+// Half-tile accumulator (per CTA, per-SM M = 64): TMEM lanes 0-63 hold the
+// CTA's 64 rows for output columns [0, BN/2), lanes 64-127 the same rows for
+// columns [BN/2, BN), both in TMEM columns [0, BN/2) of the accumulator.
 // SCATTER (grouped only): the expert-parallel epilogue of gemm_tc_kernel —
 // packed row l goes to its token owner's buffer (possibly a peer GPU's).
 template <int BN, typename OutT, bool ROWSCALE = false, bool GROUPED = false, bool SCATTER = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    GemmTcArgs args) {
+                    const __grid_constant__ CUtensorMap tmA64, GemmTcArgs args) {
   using Shape = GemmTc2Shape<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -97,20 +101,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if constexpr (GROUPED) tma_prefetch_desc(&tmA64);
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_holder, Shape::kTmemCols);
     tmem_relinquish_pair();
   }
+  pdl_allow_next();
+  pdl_wait();
   if constexpr (GROUPED) {
-    pdl_wait();
-    pdl_allow_next();
-    // Every CTA builds the same schedule; the epilogue staging area is free
-    // until the first tile and serves as scan scratch.
-    build_grouped_schedule(args, nn, sched, reinterpret_cast<int*>(sEpi), 2 * kGemmBM);
-  } else {
-    pdl_allow_next();
-    pdl_wait();
+    // Every CTA builds the same schedule (warp 0; cluster_sync publishes it).
+    build_grouped_schedule(args, nn, sched, threadIdx.x < 32, 2 * kGemmBM);
   }
   tc_fence_before();
   cluster_sync();  // both CTAs' barriers initialised, TMEM allocated, schedule built
@@ -154,9 +155,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             break;
           }
           const uint32_t full_leader = map_shared(smem_addr(&full[stage]), 0);
-          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * Shape::kStageBytes);
-          tma_load_2d_pair(sA + stage * kGemmABytes, &tmA, full_leader, kb * kGemmBK,
-                           tc.a_row + static_cast<int>(rank) * kGemmBM);
+          const bool half = GROUPED && tc.rows_valid <= kGemmBM;
+          if (leader)
+            mbar_arrive_expect_tx(&full[stage], 2 * (half ? kGemmABytes / 2 + Shape::kBBytes
+                                                          : Shape::kStageBytes));
+          if (half) {
+            tma_load_2d_pair(sA + stage * kGemmABytes, &tmA64, full_leader, kb * kGemmBK,
+                             tc.a_row + static_cast<int>(rank) * (kGemmBM / 2));
+          } else {
+            tma_load_2d_pair(sA + stage * kGemmABytes, &tmA, full_leader, kb * kGemmBK,
+                             tc.a_row + static_cast<int>(rank) * kGemmBM);
+          }
 #pragma unroll
           for (int c = 0; c < Shape::kBHalf / 64; ++c) {
             const int col = tc.n0 + static_cast<int>(rank) * Shape::kBHalf + c * 64;
@@ -178,12 +187,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (leader only)
     if (leader && lane == 0) {
-      const uint32_t idesc = args.idesc;
       int stage = 0;
       uint32_t phase = 0;
       int i = 0;
       bool ok = true;
       for (int t = pair; t < ntiles && ok; t += npairs, ++i) {
+        uint32_t idesc = args.idesc;
+        if constexpr (GROUPED) {
+          if (tile_at(t).rows_valid <= kGemmBM) idesc = args.idesc_half;
+        }
         const int acc = i & 1;
         const uint32_t acc_phase = (static_cast<uint32_t>(i) >> 1) & 1u;
         if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, abort_flag, 12)) break;
@@ -230,11 +242,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      // This CTA's accumulator rows are tile rows [128 rank, 128 rank + 128).
-      const int local = static_cast<int>(rank) * kGemmBM + r;
+      // Full tile: this CTA's accumulator rows are tile rows [128 rank, +128),
+      // warp quadrant q holds rows 32 q .. 32 q + 31, all BN columns.
+      // Half tile (grouped): this CTA's rows are [64 rank, +64); quadrant q holds
+      // rows 32 (q & 1) .. +31 of column half q >> 1 (BN / 2 columns each).
+      const bool half = GROUPED && tc.rows_valid <= kGemmBM;
+      const int local = half ? static_cast<int>(rank) * (kGemmBM / 2) + (q & 1) * 32 + lane
+                             : static_cast<int>(rank) * kGemmBM + r;
+      const int col0 = tc.n0 + (half ? (q >> 1) * (BN / 2) : 0);
       bool row_ok = local < tc.rows_valid;
       const int row = tc.c_row + local;
-      OutT* crow = row_ok ? C + static_cast<size_t>(row) * N + tc.n0 : nullptr;
+      OutT* crow = row_ok ? C + static_cast<size_t>(row) * N + col0 : nullptr;
       if constexpr (SCATTER) {
         if (row_ok) {
           const int a = args.rowmap[row];
@@ -244,7 +262,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             crow = nullptr;
           } else {
             crow = reinterpret_cast<OutT*>(args.out_ptrs[o]) +
-                   static_cast<size_t>(a - o * args.rows_per_owner) * N + tc.n0;
+                   static_cast<size_t>(a - o * args.rows_per_owner) * N + col0;
           }
         }
       }
@@ -252,7 +270,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       float scale = 1.f;
       if constexpr (ROWSCALE) scale = row_ok ? args.row_scale[row] : 1.f;
       __syncwarp();
-      epilogue_store_tile<BN, OutT, ROWSCALE>(taddr, stage, rowptr, tc.n0, N, lane, scale);
+      if (half) {
+        epilogue_store_tile<BN / 2, OutT, ROWSCALE>(taddr, stage, rowptr, col0, N, lane, scale);
+      } else {
+        epilogue_store_tile<BN, OutT, ROWSCALE>(taddr, stage, rowptr, col0, N, lane, scale);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(map_shared(smem_addr(&tempty[acc]), 0));

@@ -143,7 +143,8 @@ def test_tcgen05_grouped_gemm_ragged_experts(counts, offset_dtype, cuda_device):
 @pytest.mark.parametrize("experts", [191, 193, 300, 1000])
 def test_grouped_gemm_balanced_raster_many_experts(experts, cuda_device):
     """RASTER 2 (low-reuse experts interleaved) computes the same tiles as
-    RASTER 1, bit for bit, with the schedule scan spread over every thread."""
+    RASTER 1, bit for bit; experts not a multiple of 32 exercise uneven runs
+    per lane of the warp that builds the schedule."""
     n, k = 136, 72
     rng = np.random.default_rng(experts)
     counts = rng.integers(0, 400, size=experts)
@@ -170,11 +171,12 @@ def test_grouped_gemm_balanced_raster_many_experts(experts, cuda_device):
                                     {"BLOCK_N": 128, "num_stages": 8, "CTA_GROUP": 2},
                                     {"BLOCK_N": 256, "num_stages": 4, "CTA_GROUP": 2,
                                      "RASTER": 2}])
-def test_grouped_gemm_pair_split_covers_every_row(params, cuda_device):
-    """CTA_GROUP 2: pair tiles take each expert's rows but a <= 128-row tail,
-    a single-CTA launch takes the tails.  Expert sizes around every multiple of
-    128 and 256; every row of the NaN-prefilled output is written exactly as
-    the oracle says, and rows before offsets[0] / after offsets[E] stay NaN."""
+def test_grouped_gemm_pair_tiles_cover_every_row(params, cuda_device):
+    """CTA_GROUP 2: 256-row pair tiles per expert, a last block of <= 128 rows
+    as a half-height pair tile (M = 128, 64 rows per CTA).  Expert sizes around
+    every multiple of 128 and 256; every row of the NaN-prefilled output is
+    written exactly as the oracle says, rows before offsets[0] / after
+    offsets[E] stay NaN, and the single-CTA kernel agrees."""
     n, k = 392, 200
     sizes = [0, 1, 127, 128, 129, 255, 256, 257, 383, 384, 385, 511, 512, 513, 700, 1000]
     rng = np.random.default_rng(1)
