@@ -153,25 +153,6 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-// L2 policy that marks the lines a load brings in as first to evict (operands
-// used once: streaming them must not push reused tiles out of L2).
-__device__ __forceinline__ uint64_t l2_policy_evict_first() {
-  uint64_t policy;
-  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
-  return policy;
-}
-
-__device__ __forceinline__ void tma_load_3d_hint(void* dst, const CUtensorMap* map, uint64_t* bar,
-                                                 int32_t c0, int32_t c1, int32_t c2,
-                                                 uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_addr(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(c0), "r"(c1), "r"(c2),
-      "l"(policy)
-      : "memory");
-}
-
 // ---------------------------------------------------------------------------
 // tcgen05: TMEM allocation, MMA issue/commit, TMEM -> register loads.
 // ---------------------------------------------------------------------------

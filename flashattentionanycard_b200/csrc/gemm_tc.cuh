@@ -198,26 +198,57 @@ __device__ __forceinline__ int warp_exclusive_scan(int v, int lane, int* total) 
   return x - v;
 }
 
-// Build the schedule with warp 0 of the CTA (lane i owns a contiguous run of
-// experts, one warp-shuffle scan per count; no block barrier inside: the
-// caller's barrier publishes the schedule).  `warp0` selects the building
-// warp; other threads return at once.
+// Build the grouped schedule; every thread of the CTA calls this.  Expert
+// order (the default): every thread loads its experts' offsets once (one
+// round of global loads in parallel), then warp 0 turns the per-expert tile
+// counts into the prefix with a chunked warp scan.  Balanced order: warp 0
+// alone sorts the experts into the two reuse classes while it scans.  Ends
+// without a barrier: the caller's barrier publishes the schedule.
 __device__ __forceinline__ void build_grouped_schedule(const GemmTcArgs& args, int nn,
-                                                       const GroupedSchedule& g, bool warp0,
+                                                       const GroupedSchedule& g,
                                                        int tile_rows = kGemmBM) {
-  if (!warp0) return;
   const int lane = threadIdx.x & 31;
+  const bool warp0 = threadIdx.x < 32;
   const int E = args.E;
   const int per = (E + 31) / 32;
   const int e0 = min(E, lane * per);
   const int e1 = min(E, e0 + per);
-  const bool balanced = args.raster == kRasterBalanced;
+  if (args.raster != kRasterBalanced) {
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+      int st, c;
+      expert_rows(args, e, &st, &c);
+      g.pstart[e] = st;
+      g.pcount[e] = c;
+      g.pexp[e] = e;
+      g.pre[e] = ((c + tile_rows - 1) / tile_rows) * nn;  // tiles, turned into the prefix below
+    }
+    __syncthreads();
+    if (warp0) {
+      int sum = 0;
+      for (int e = e0; e < e1; ++e) sum += g.pre[e];
+      int total;
+      int run = warp_exclusive_scan(sum, lane, &total);
+      for (int e = e0; e < e1; ++e) {
+        const int tiles = g.pre[e];
+        g.pre[e] = run;
+        run += tiles;
+      }
+      if (lane == 0) {
+        g.pre[E] = total;
+        g.totals[0] = total;
+        g.totals[1] = 0;
+        g.totals[2] = E;
+      }
+    }
+    return;
+  }
+  if (!warp0) return;
   int he = 0, le = 0, ht = 0, lt = 0;
   for (int e = e0; e < e1; ++e) {
     int st, c;
     expert_rows(args, e, &st, &c);
     const int mb = (c + tile_rows - 1) / tile_rows;
-    if (balanced && mb <= kLowReuseMBlocks) {
+    if (mb <= kLowReuseMBlocks) {
       ++le;
       lt += mb * nn;
     } else {
@@ -241,7 +272,7 @@ __device__ __forceinline__ void build_grouped_schedule(const GemmTcArgs& args, i
     expert_rows(args, e, &st, &c);
     const int mb = (c + tile_rows - 1) / tile_rows;
     int pos;
-    if (balanced && mb <= kLowReuseMBlocks) {
+    if (mb <= kLowReuseMBlocks) {
       pos = lpos++;
       g.pre[pos] = ltile;
       ltile += mb * nn;
@@ -257,8 +288,7 @@ __device__ __forceinline__ void build_grouped_schedule(const GemmTcArgs& args, i
 }
 
 __device__ __forceinline__ TileCoord grouped_tile(int t, const GroupedSchedule& g, int E, int nn,
-                                                  int bn, int raster, bool* low,
-                                                  int tile_rows = kGemmBM) {
+                                                  int bn, int raster, int tile_rows = kGemmBM) {
   const int total = g.totals[0];
   const int nlow = g.totals[1];
   int u = t;
@@ -291,7 +321,6 @@ __device__ __forceinline__ TileCoord grouped_tile(int t, const GroupedSchedule& 
   c.expert = g.pexp[lo];
   c.c_row = c.a_row;
   c.rows_valid = min(tile_rows, count - mb * tile_rows);
-  *low = lo >= g.totals[2];
   return c;
 }
 
@@ -353,7 +382,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   int ntiles;
   if constexpr (GROUPED) {
-    build_grouped_schedule(args, nn, sched, threadIdx.x < 32);
+    build_grouped_schedule(args, nn, sched);
   }
   tc_fence_before();
   __syncthreads();
@@ -365,11 +394,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     ntiles = ((args.M + kGemmBM - 1) / kGemmBM) * nn;
   }
 
-  auto tile_at = [&](int t, bool* low) -> TileCoord {
+  auto tile_at = [&](int t) -> TileCoord {
     if constexpr (GROUPED) {
-      return grouped_tile(t, sched, args.E, nn, BN, args.raster, low);
+      return grouped_tile(t, sched, args.E, nn, BN, args.raster);
     } else {
-      *low = false;
       return dense_tile(t, args.M, nn, args.group_m, BN);
     }
   };
@@ -380,10 +408,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      const uint64_t evict_first = l2_policy_evict_first();
       for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-        bool low;
-        const TileCoord tc = tile_at(t, &low);
+        const TileCoord tc = tile_at(t);
         for (int kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, 1)) {
             ok = false;
@@ -396,15 +422,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int c = 0; c < BN / 64; ++c) {
             if constexpr (GROUPED) {
-              // Weights of a low-reuse expert are read by at most two tiles:
-              // stream them past L2 residents.
-              if (low) {
-                tma_load_3d_hint(b_dst + c * 8192, &tmB, &full[stage], tc.n0 + c * 64,
-                                 kb * kGemmBK, tc.expert, evict_first);
-              } else {
-                tma_load_3d(b_dst + c * 8192, &tmB, &full[stage], tc.n0 + c * 64, kb * kGemmBK,
-                            tc.expert);
-              }
+              tma_load_3d(b_dst + c * 8192, &tmB, &full[stage], tc.n0 + c * 64, kb * kGemmBK,
+                          tc.expert);
             } else {
               tma_load_2d(b_dst + c * 8192, &tmB, &full[stage], tc.n0 + c * 64, kb * kGemmBK);
             }
@@ -465,8 +484,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     OutT** rowptr = reinterpret_cast<OutT**>(sEpi + kEpiWarps * kEpiStageBytes) + (warp - 2) * 32;
     int i = 0;
     for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
-      bool low;
-      const TileCoord tc = tile_at(t, &low);
+      const TileCoord tc = tile_at(t);
       const int acc = i & 1;
       const uint32_t acc_phase = (static_cast<uint32_t>(i) >> 1) & 1u;
       const bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, 4);

@@ -110,8 +110,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   pdl_allow_next();
   pdl_wait();
   if constexpr (GROUPED) {
-    // Every CTA builds the same schedule (warp 0; cluster_sync publishes it).
-    build_grouped_schedule(args, nn, sched, threadIdx.x < 32, 2 * kGemmBM);
+    // Every CTA builds the same schedule (cluster_sync publishes it).
+    build_grouped_schedule(args, nn, sched, 2 * kGemmBM);
   }
   tc_fence_before();
   cluster_sync();  // both CTAs' barriers initialised, TMEM allocated, schedule built
@@ -123,8 +123,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // grouped inside each expert (rows_valid = rows of the expert in the tile).
   auto tile_at = [&](int t) -> TileCoord {
     if constexpr (GROUPED) {
-      bool low;
-      return grouped_tile(t, sched, args.E, nn, BN, args.raster, &low, 2 * kGemmBM);
+      return grouped_tile(t, sched, args.E, nn, BN, args.raster, 2 * kGemmBM);
     } else {
       const int per_group = args.group_m * nn;
       const int group = t / per_group;

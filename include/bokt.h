@@ -74,9 +74,8 @@ extern "C" {
  *   GEMM                : cta_group 2 runs CTA pairs (tcgen05 cta_group::2, 256-row tiles)
  *   grouped GEMM        : raster 1 (the default) runs the tiles expert by expert;
  *                         raster 2 spreads the tiles of experts with at most two
- *                         128-row blocks evenly between the others, so their
- *                         once-read weights stream (L2 evict-first) while other
- *                         tiles compute
+ *                         row blocks evenly between the others, so their
+ *                         once-read weights stream while other tiles compute
  */
 typedef struct bokt_params {
   int32_t block_m;
