@@ -639,7 +639,10 @@ class MoeLarge:
         import torch
 
         torch.cuda.empty_cache()
-        self.graphable = False  # collectives between kernels: timed eagerly
+        # Collectives between kernels: timed eagerly.  (Capturing the peer
+        # path's steps, NCCL collectives included, in CUDA graphs hung a 2-GPU
+        # run until its outer timeout; the cause was not found.)
+        self.graphable = False
         rows = int(self.placement.rank_rows[rank])
         self.kernel_flops = 2.0 * rows * cfg["k"] * cfg["n"]
 
