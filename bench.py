@@ -295,7 +295,7 @@ class Gemm:
         from flashattentionanycard_b200 import workloads
         from flashattentionanycard_b200.configs.search_spaces import default_params
 
-        self.name = f"gemm{size}"
+        self.name = f"gemm{size}" + ("_fp16" if dtype == "fp16" else "")
         self.dtype = dtype
         self.size = size
         self.params = default_params("gemm")
@@ -738,11 +738,14 @@ WORKLOADS = {
     "rmsnorm": lambda d, r, w: Rmsnorm(d, r, w),
     "gemm8192": lambda d, r, w: Gemm(d, r, w, 8192, "bf16", split=True),
     "gemm2048": lambda d, r, w: Gemm(d, r, w, 2048, "bf16", split=False),
+    "gemm8192_fp16": lambda d, r, w: Gemm(d, r, w, 8192, "fp16", split=True),
+    "gemm2048_fp16": lambda d, r, w: Gemm(d, r, w, 2048, "fp16", split=False),
     "moe_small": lambda d, r, w: MoeSmall(d, r, w),
     "moe_large": lambda d, r, w: MoeLarge(d, r, w),
     "rmsnorm_gemm": lambda d, r, w: RmsnormGemm(d, r, w),
 }
-DEFAULT_STEPS = {"rmsnorm": 4000, "gemm8192": 200, "gemm2048": 2000, "moe_small": 4000,
+DEFAULT_STEPS = {"rmsnorm": 4000, "gemm8192": 200, "gemm2048": 2000, "gemm8192_fp16": 200,
+                 "gemm2048_fp16": 2000, "moe_small": 4000,
                  "moe_large": 100, "rmsnorm_gemm": 400}
 
 
@@ -837,11 +840,12 @@ def _cpu_only_workload(name):
         w.cpu_config = lambda: {"workload": f"rmsnorm_bf16_{w.m}x{w.n}_eps1e-6",
                                 "sample": "full 4096x4096 per step"}
         return w
-    if name in ("gemm8192", "gemm2048"):
+    if name.startswith("gemm") and not name.startswith("gemm_"):
         w = Gemm.__new__(Gemm)
-        w.size = 8192 if name == "gemm8192" else 2048
-        w.name, w.dtype, w.n_local = name, "bf16", w.size
-        w.cpu_config = lambda: {"workload": f"gemm_bf16_{w.size}^3",
+        w.size = 8192 if name.startswith("gemm8192") else 2048
+        w.dtype = "fp16" if name.endswith("_fp16") else "bf16"
+        w.name, w.n_local = name, w.size
+        w.cpu_config = lambda: {"workload": f"gemm_{w.dtype}_{w.size}^3",
                                 "sample": f"{256 if w.size > 2048 else w.size} rows of A per step"}
         return w
     if name == "moe_small":
@@ -1095,7 +1099,8 @@ def run_ours(args):
         dist.destroy_process_group()
     if rank != 0:
         return 0
-    scaling = "weak" if args.workload in ("rmsnorm", "gemm2048", "moe_small") else "strong"
+    scaling = ("weak" if args.workload in ("rmsnorm", "gemm2048", "gemm2048_fp16", "moe_small")
+               else "strong")
     line = {
         "metric": METRIC, "value": value, "unit": workload.unit, "n_gpus": world,
         "steps": steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
