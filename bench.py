@@ -523,7 +523,7 @@ class MoeSmall:
         self.sm = torch.cuda.get_device_properties(device).multi_processor_count
 
     def dominant_kernel(self, i):
-        """The grouped GEMM call (pair + tail launches when CTA_GROUP is 2)."""
+        """The grouped GEMM call (one launch: single CTAs, or CTA pairs when CTA_GROUP is 2)."""
         self.step(i)
 
     def step(self, i):

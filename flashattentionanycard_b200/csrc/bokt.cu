@@ -174,17 +174,17 @@ int encode_map(CUtensorMap* map, const void* base, int rank, const uint64_t* dim
 // ----------------------------------------------------------------- GEMM dispatch
 using bokt::GemmTcArgs;
 
-template <int BN, bool GROUPED, typename T, bool SCATTER, bool NORM = false>
+template <int BN, bool GROUPED, typename T, bool SCATTER, bool ROWSCALE = false>
 const void* tc_kernel_ptr() {
-  return reinterpret_cast<const void*>(&bokt::gemm_tc_kernel<BN, GROUPED, T, SCATTER, NORM>);
+  return reinterpret_cast<const void*>(&bokt::gemm_tc_kernel<BN, GROUPED, T, SCATTER, ROWSCALE>);
 }
 
-template <bool GROUPED, typename T, bool SCATTER, bool NORM = false>
+template <bool GROUPED, typename T, bool SCATTER, bool ROWSCALE = false>
 const void* tc_kernel_for(int bn) {
   switch (bn) {
-    case 64: return tc_kernel_ptr<64, GROUPED, T, SCATTER, NORM>();
-    case 128: return tc_kernel_ptr<128, GROUPED, T, SCATTER, NORM>();
-    case 256: return tc_kernel_ptr<256, GROUPED, T, SCATTER, NORM>();
+    case 64: return tc_kernel_ptr<64, GROUPED, T, SCATTER, ROWSCALE>();
+    case 128: return tc_kernel_ptr<128, GROUPED, T, SCATTER, ROWSCALE>();
+    case 256: return tc_kernel_ptr<256, GROUPED, T, SCATTER, ROWSCALE>();
   }
   return nullptr;
 }
