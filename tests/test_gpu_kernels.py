@@ -171,7 +171,8 @@ def test_grouped_gemm_balanced_raster_many_experts(experts, cuda_device):
                                     {"BLOCK_N": 128, "num_stages": 8, "CTA_GROUP": 2},
                                     {"BLOCK_N": 256, "num_stages": 4, "CTA_GROUP": 2,
                                      "RASTER": 2}])
-def test_grouped_gemm_pair_tiles_cover_every_row(params, cuda_device):
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+def test_grouped_gemm_pair_tiles_cover_every_row(params, dtype, cuda_device):
     """CTA_GROUP 2: 256-row pair tiles per expert, a last block of <= 128 rows
     as a half-height pair tile (M = 128, 64 rows per CTA).  Expert sizes around
     every multiple of 128 and 256; every row of the NaN-prefilled output is
@@ -187,10 +188,11 @@ def test_grouped_gemm_pair_tiles_cover_every_row(params, cuda_device):
         starts.append(starts[-1] + c)
     rows = starts[-1] + trail
     g = torch.Generator().manual_seed(7)
-    x = torch.randn(rows, k, generator=g).bfloat16()
-    w = (0.5 * torch.randn(len(counts), k, n, generator=g)).bfloat16()
+    tdt = torch.bfloat16 if dtype == "bf16" else torch.float16
+    x = torch.randn(rows, k, generator=g).to(tdt)
+    w = (0.5 * torch.randn(len(counts), k, n, generator=g)).to(tdt)
     ref = numerics.grouped_gemm_fp32(as_f32(x), as_f32(w), starts)
-    out = nan_like((rows, n), "bf16", cuda_device)
+    out = nan_like((rows, n), dtype, cuda_device)
     offsets = torch.tensor(starts, dtype=torch.int64, device=cuda_device)
     compiled = moe_grouped_gemm.launch(x.to(cuda_device), w.to(cuda_device), offsets, out,
                                        params, 148)
@@ -198,8 +200,8 @@ def test_grouped_gemm_pair_tiles_cover_every_row(params, cuda_device):
     assert compiled.path == "tcgen05" and compiled.n_spills == 0
     got = out.float().cpu().numpy()
     assert np.isnan(got[:lead]).all() and np.isnan(got[rows - trail:]).all()
-    gate(out[lead:rows - trail], ref[lead:rows - trail], "bf16")
-    single = nan_like((rows, n), "bf16", cuda_device)
+    gate(out[lead:rows - trail], ref[lead:rows - trail], dtype)
+    single = nan_like((rows, n), dtype, cuda_device)
     moe_grouped_gemm.launch(x.to(cuda_device), w.to(cuda_device), offsets, single,
                             dict(params, CTA_GROUP=1, num_stages=4), 148)
     torch.cuda.synchronize()
