@@ -138,15 +138,15 @@ def test_nccl_two_ranks(cuda_device):
     assert "EP_NCCL_OK" in run.stdout
 
 
-def build_peer_ranks(world, tokens, experts, k, n, seed, device):
+def build_peer_ranks(world, tokens, experts, k, n, seed, device, dtype=torch.bfloat16):
     ids_cpu = zipf_routing(tokens, experts, 2, 1.1, seed).reshape(-1)
     ids = ids_cpu.numpy()
     placement = ep.plan_placement(np.bincount(ids, minlength=experts), world)
     tpr = tokens // world
     plan = ep.plan_splits(ids, placement, 2, tpr)
     g = torch.Generator().manual_seed(seed)
-    x = torch.randn(tokens, k, generator=g).bfloat16()
-    w = (0.05 * torch.randn(experts, k, n, generator=g)).bfloat16()
+    x = torch.randn(tokens, k, generator=g).to(dtype)
+    w = (0.05 * torch.randn(experts, k, n, generator=g)).to(dtype)
     wd = w.to(device)
     ranks = [ep.PeerExpertParallelMoE(wd[ep.local_weight_slices(placement, r)].contiguous(),
                                       placement, plan, r, world, 2, tpr, exchange=False)
@@ -158,13 +158,14 @@ def build_peer_ranks(world, tokens, experts, k, n, seed, device):
     return ids_cpu, ids, x, w, placement, ranks
 
 
-@pytest.mark.parametrize("world", [2, 4, 8])
-def test_peer_path_virtual_ranks_on_one_gpu(world, cuda_device):
+@pytest.mark.parametrize("world,dtype", [(2, "bf16"), (4, "bf16"), (8, "bf16"), (4, "fp16")])
+def test_peer_path_virtual_ranks_on_one_gpu(world, dtype, cuda_device):
     """Dispatch stores and the scatter epilogue write into other ranks' buffers
     (here: other buffers of the same GPU); the result must equal the oracle."""
     tokens, experts, k, n = 4096, 32, 256, 512
+    tdt = torch.bfloat16 if dtype == "bf16" else torch.float16
     ids_cpu, ids, x, w, placement, ranks = build_peer_ranks(world, tokens, experts, k, n, 11,
-                                                            cuda_device)
+                                                            cuda_device, tdt)
     _native.device_status(reset=True)
     tpr = tokens // world
     ids_dev = ids_cpu.to(cuda_device).to(torch.int32)
@@ -184,7 +185,7 @@ def test_peer_path_virtual_ranks_on_one_gpu(world, cuda_device):
         assert m.rank_rows.cpu().tolist() == [int(v) for v in placement.rank_rows]
         a = np.arange(r * tpr * 2, (r + 1) * tpr * 2)
         ref = np.einsum("ak,akn->an", xf[a // 2], wf[ids[a]])
-        gate(m.out, ref, "bf16")
+        gate(m.out, ref, dtype)
 
 
 def test_peer_path_single_rank_forward(cuda_device):
