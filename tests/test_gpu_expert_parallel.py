@@ -20,6 +20,7 @@ import torch
 
 from flashattentionanycard_b200 import _native
 from flashattentionanycard_b200 import expert_parallel as ep
+from flashattentionanycard_b200.configs.search_spaces import default_params
 from flashattentionanycard_b200.workloads import zipf_routing
 from oracle import numerics
 from oracle import expert_parallel as oracle_ep
@@ -138,7 +139,8 @@ def test_nccl_two_ranks(cuda_device):
     assert "EP_NCCL_OK" in run.stdout
 
 
-def build_peer_ranks(world, tokens, experts, k, n, seed, device, dtype=torch.bfloat16):
+def build_peer_ranks(world, tokens, experts, k, n, seed, device, dtype=torch.bfloat16,
+                     params=None):
     ids_cpu = zipf_routing(tokens, experts, 2, 1.1, seed).reshape(-1)
     ids = ids_cpu.numpy()
     placement = ep.plan_placement(np.bincount(ids, minlength=experts), world)
@@ -149,7 +151,8 @@ def build_peer_ranks(world, tokens, experts, k, n, seed, device, dtype=torch.bfl
     w = (0.05 * torch.randn(experts, k, n, generator=g)).to(dtype)
     wd = w.to(device)
     ranks = [ep.PeerExpertParallelMoE(wd[ep.local_weight_slices(placement, r)].contiguous(),
-                                      placement, plan, r, world, 2, tpr, exchange=False)
+                                      placement, plan, r, world, 2, tpr, params=params,
+                                      exchange=False)
              for r in range(world)]
     xpk = [m.x_packed.data_ptr() for m in ranks]
     outs = [m.out.data_ptr() for m in ranks]
@@ -158,14 +161,20 @@ def build_peer_ranks(world, tokens, experts, k, n, seed, device, dtype=torch.bfl
     return ids_cpu, ids, x, w, placement, ranks
 
 
-@pytest.mark.parametrize("world,dtype", [(2, "bf16"), (4, "bf16"), (8, "bf16"), (4, "fp16")])
-def test_peer_path_virtual_ranks_on_one_gpu(world, dtype, cuda_device):
+@pytest.mark.parametrize("world,dtype,kernel", [(2, "bf16", "single"), (4, "bf16", "single"),
+                                               (8, "bf16", "single"), (4, "fp16", "single"),
+                                               (4, "bf16", "pairs"), (8, "bf16", "pairs"),
+                                               (2, "fp16", "pairs")])
+def test_peer_path_virtual_ranks_on_one_gpu(world, dtype, kernel, cuda_device):
     """Dispatch stores and the scatter epilogue write into other ranks' buffers
-    (here: other buffers of the same GPU); the result must equal the oracle."""
+    (here: other buffers of the same GPU); the result must equal the oracle.
+    ``single``: the library defaults (single-CTA grouped GEMM); ``pairs``: the
+    MoE default parameters (CTA-pair grouped GEMM with half-height tails)."""
     tokens, experts, k, n = 4096, 32, 256, 512
     tdt = torch.bfloat16 if dtype == "bf16" else torch.float16
+    params = default_params("moe_grouped_gemm") if kernel == "pairs" else None
     ids_cpu, ids, x, w, placement, ranks = build_peer_ranks(world, tokens, experts, k, n, 11,
-                                                            cuda_device, tdt)
+                                                            cuda_device, tdt, params)
     _native.device_status(reset=True)
     tpr = tokens // world
     ids_dev = ids_cpu.to(cuda_device).to(torch.int32)
