@@ -1,29 +1,44 @@
 """Benchmark of the bo-kernel-tuner hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload rmsnorm|gemm8192|gemm2048|moe_small|moe_large]
+                    [--workload NAME] [--secondary auto|none|NAME,NAME...]
 
-Prints ONE JSON line (rank 0).  A step is one pass of the workload's hot path
+Prints ONE JSON line (rank 0).  A step is one pass of a workload's hot path
 over one batch of synthetic input already resident in HBM; K steps are
 captured in CUDA graphs and replayed between a barrier + synchronize on both
-sides, timed with CUDA events on the launching stream, max over ranks.
+sides (an untimed replay runs right before the timed one, so the GPU is busy
+and at clock when the start event is recorded), timed with CUDA events on the
+launching stream, max over ranks.
 
-Workloads (default ``rmsnorm``, the 4096 x 4096 bf16 RMSNorm):
+The headline workload (``--workload``, default ``rmsnorm``) gives the line's
+top-level ``value``; with the default ``--secondary auto`` the same run also
+times the 8192^3 GEMM and the 64-expert MoE step and reports each of them under
+``secondary`` with its own roofline, end-to-end rate, CPU baseline, clocks and
+parity check.
+
+Workloads:
   rmsnorm    x[4096,4096] bf16 per rank (rows of a G*4096-row matrix split
              across G ranks, no collective: weak scaling); GB/s.
   gemm8192   C = A.B bf16 8192^3; B and C split along N across ranks (A
              replicated, no collective: strong scaling); TFLOP/s.
-  gemm2048   2048^3 bf16, replicas; TFLOP/s.
+  gemm2048   2048^3 bf16, replicas; TFLOP/s.  (``_fp16`` variants of both.)
   moe_small  8-expert grouped GEMM, 1528 tokens, replicas; TFLOP/s.
-  moe_large  64 experts x [4096, 14336], 16384 tokens top-2 Zipf(1.1),
-             one GPU: device routing + gather + grouped GEMM; TFLOP/s.
+  moe_large  64 experts x [4096, 14336], 16384 tokens top-2 Zipf(1.1):
+             one GPU: device routing + gather + grouped GEMM; N GPUs: expert
+             parallel with NVLink peer-store dispatch and combine; TFLOP/s.
+  rmsnorm_gemm  RMSNorm fused into the 4096 -> 14336 projection; TFLOP/s.
 
-Inputs larger than L2 (126 MB) or rotated through buffer sets that together
-exceed it, so every step reads from HBM.  ``--impl reference`` times the
-reference's FP32 CPU path (the oracle port, numpy) on the host cores.
+Every workload checks its own output after timing (sampled rows against a
+torch fp32 computation on the device, TF32 off, with the reference's gate
+tolerances) and reports ``parity``; a mismatch makes the run exit non-zero.
+Inputs are larger than L2 (126 MB) or rotated through buffer sets that
+together exceed it, so every step reads from HBM.  ``--impl reference`` times
+the reference's FP32 CPU path (the oracle port, numpy) on the host cores with
+the same ``config`` dicts.
 """
 
 import argparse
+import gc
 import json
 import math
 import os
@@ -43,8 +58,10 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 L2_BYTES = 126 * 1024 * 1024
 EP_COMM = "peer"  # --ep-comm: expert-parallel dispatch/combine over NVLink peer stores or NCCL
 MOE_EXPERTS = None  # --experts: moe_large with fewer experts (small profiling case)
+PARAM_OVERRIDES = {}  # --params: launch-parameter overrides for the timed workloads
 # Rotating input sets together span 4x L2, so a set is long evicted when it is reused.
 ROTATION_BYTES = 4 * L2_BYTES
+SECONDARY_AUTO = ("gemm8192", "moe_large")
 
 
 # ----------------------------------------------------------------------------- utilities
@@ -101,17 +118,13 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append((time.perf_counter(), line.strip()))
 
-    def stop(self, t0, t1):
+    def window(self, t0, t1):
+        """Clock summary of the samples taken in [t0, t1] (widened by 0.15 s each side)."""
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        time.sleep(0.12)
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        window = [line for t, line in self.lines if t0 - 0.15 <= t <= t1 + 0.15] or \
-                 [line for _, line in self.lines]
+        lines = list(self.lines)
+        window = [line for t, line in lines if t0 - 0.15 <= t <= t1 + 0.15] or \
+                 [line for _, line in lines[-5:]]
         sm, smax, reasons = [], [], set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
         for line in window:
@@ -133,11 +146,21 @@ class ClockSampler:
             "samples": len(sm),
         }
 
+    def stop(self):
+        if self.proc is None:
+            return
+        time.sleep(0.2)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+
 
 def graph_time_ms(stream, fn, count, reps=3):
     """Average device time of ``fn`` (one kernel launch) over ``count`` launches
     captured in one CUDA graph, timed with CUDA events on ``stream``; best of
-    ``reps`` replays."""
+    ``reps`` replays, each preceded by an untimed replay."""
     import torch
 
     graph = torch.cuda.CUDAGraph()
@@ -149,6 +172,8 @@ def graph_time_ms(stream, fn, count, reps=3):
     best = None
     for _ in range(reps):
         b, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            graph.replay()  # untimed: the timed replay starts on a busy GPU
         b.record(stream)
         with torch.cuda.stream(stream):
             graph.replay()
@@ -164,8 +189,6 @@ def paired_graph_times(stream, fn_a, fn_b, count=20, reps=9):
     """Median per-step device time of two step functions, each captured as a
     graph of ``count`` steps and replayed alternately (a, b, a, b, ...) so that
     clock and power drift affect both alike; CUDA events on ``stream``."""
-    import statistics
-
     import torch
 
     graphs = []
@@ -197,6 +220,178 @@ def cpu_threads():
     return os.cpu_count() or 1
 
 
+def params_for(kernel, **fixed):
+    """Default launch parameters of ``kernel`` with bench overrides (--params) applied."""
+    from flashattentionanycard_b200.configs.search_spaces import default_params
+
+    p = dict(default_params(kernel), **fixed)
+    p.update(PARAM_OVERRIDES.get(kernel, {}))
+    return p
+
+
+# ----------------------------------------------------------------------------- parity
+def gate_check(out, ref, dtype):
+    """The reference's FP32 gate (tuner/worker.py:108-116 of the reference:
+    finite outputs, |out - ref| <= atol + rtol |ref| with (rtol, atol) = (0.01,
+    0.02) for fp16 and (0.02, 0.15) for bf16) plus a normwise relative error
+    ||out - ref|| / ||ref|| <= 1e-2."""
+    import torch
+
+    rtol, atol = (0.01, 0.02) if dtype == "fp16" else (0.02, 0.15)
+    o, r = out.float(), ref.float()
+    finite = bool(torch.isfinite(o).all()) and bool(torch.isfinite(r).all())
+    diff = (o - r).abs()
+    within = bool((diff <= atol + rtol * r.abs()).all())
+    norm_r = float(torch.linalg.vector_norm(r))
+    normwise = float(torch.linalg.vector_norm(o - r)) / max(norm_r, 1e-30)
+    return {"ok": finite and within and normwise <= 1e-2,
+            "max_abs_error": float(diff.max()) if diff.numel() else 0.0,
+            "normwise_rel_error": normwise, "rtol": rtol, "atol": atol}
+
+
+def fp32_reference_mode():
+    import torch
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False
+    torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = False
+
+
+def sample_rows(n, count, seed=0):
+    """``count`` distinct row indices of [0, n): both ends plus seeded picks."""
+    import random
+
+    if n <= count:
+        return list(range(n))
+    rng = random.Random(seed)
+    picks = {0, n - 1, n // 2}
+    while len(picks) < count:
+        picks.add(rng.randrange(n))
+    return sorted(picks)
+
+
+# ----------------------------------------------------------------------------- configs
+# One function per workload, computed on the CPU from the workload's sizes, so
+# the GPU arm and the --impl reference arm print the same ``config`` dict.
+def rmsnorm_config(world):
+    from flashattentionanycard_b200 import workloads
+
+    cfg = workloads.RMSNORM
+    m, n = cfg["m"], cfg["n"]
+    sets = max(2, math.ceil(ROTATION_BYTES / (2 * m * n * 2)))
+    return {"workload": f"rmsnorm_bf16_{m}x{n}_eps1e-6", "rows_per_gpu": m, "hidden": n,
+            "total_rows": m * world, "partition": "row-split, no collective",
+            "l2": f"rotating {sets} buffer sets ({sets * 2 * m * n * 2 / 2**20:.0f} MiB > L2)",
+            "params": params_for("rmsnorm")}
+
+
+def gemm_sets(size, n_local):
+    per_set = (size * size + 2 * size * n_local) * 2
+    return max(1, math.ceil(ROTATION_BYTES / per_set)) if per_set < ROTATION_BYTES else 1
+
+
+def gemm_config(size, dtype, split, world):
+    n_local = size // world if split else size
+    sets = gemm_sets(size, n_local)
+    return {"workload": f"gemm_{dtype}_{size}^3", "m": size, "k": size, "n": size,
+            "n_per_gpu": n_local,
+            "partition": "N-split, A replicated, no collective" if split else "replicas",
+            "l2": "inputs > L2" if sets == 1 else f"rotating {sets} A/C sets",
+            "params": params_for("gemm")}
+
+
+def moe_small_config(world):
+    from flashattentionanycard_b200 import workloads
+
+    counts = workloads.MOE_SMALL_COUNTS
+    k, n = workloads.MOE_SMALL["k"], workloads.MOE_SMALL["n"]
+    nonempty = sum(1 for c in counts if c)
+    per_set = (sum(counts) * k + nonempty * k * n + sum(counts) * n) * 2
+    sets = max(2, math.ceil(ROTATION_BYTES / per_set))
+    return {"workload": "moe_grouped_gemm_bf16_E8_K1024_N2048_T1528",
+            "expert_tokens": list(counts), "partition": "replicas",
+            "l2": f"rotating {sets} X/W/Y sets", "params": moe_small_params()}
+
+
+def moe_small_params():
+    # Tuned for this single-wave problem (120 tiles of 128 rows on 148 SMs):
+    # single-CTA tiles.
+    return params_for("moe_grouped_gemm", CTA_GROUP=1, num_stages=4)
+
+
+def moe_large_cfg():
+    from flashattentionanycard_b200 import workloads
+
+    cfg = dict(workloads.MOE_LARGE)
+    cfg["experts"] = MOE_EXPERTS or cfg["experts"]
+    return cfg
+
+
+def moe_large_placement(cfg, world):
+    import numpy as np
+
+    from flashattentionanycard_b200 import expert_parallel as ep
+    from flashattentionanycard_b200 import workloads
+
+    ids = workloads.zipf_routing(cfg["tokens"], cfg["experts"], cfg["topk"], cfg["zipf_s"], 0)
+    flat = ids.reshape(-1).numpy()
+    placement = ep.plan_placement(np.bincount(flat, minlength=cfg["experts"]), world)
+    return ids, placement
+
+
+def moe_large_config(world):
+    c = moe_large_cfg()
+    out = {"workload": f"moe_bf16_E{c['experts']}_K{c['k']}_N{c['n']}_T{c['tokens']}_top2_zipf1.1",
+           "partition": "single GPU (all experts local)",
+           "step": "route + gather + grouped GEMM", "l2": "W 7.5 GB > L2",
+           "params": params_for("moe_grouped_gemm")}
+    if world > 1:
+        _, p = moe_large_placement(c, world)
+        step = ("all-gather ids + route + NVLink peer-store dispatch + grouped GEMM with "
+                "peer-store combine epilogue, one-word all-reduce barriers, eager"
+                if EP_COMM == "peer" else
+                "all-gather ids + route + dispatch all-to-all + grouped GEMM + "
+                "combine all-to-all (NCCL), eager")
+        out.update({
+            "partition": f"expert-parallel over {world} GPUs: {p.virtual_experts} virtual "
+                         f"experts (hot experts replicated, rows split), LPT placement",
+            "step": step, "ep_comm": EP_COMM,
+            "rows_per_rank": [int(v) for v in p.rank_rows],
+            "max_replicas": int(p.replicas.max()),
+        })
+    return out
+
+
+def rmsnorm_gemm_config(world):
+    from flashattentionanycard_b200 import workloads
+
+    cfg = workloads.RMSNORM_GEMM
+    m, k, n = cfg["m"], cfg["k"], cfg["n"]
+    n_local = n // world
+    per_set = (m * k + k * n_local + m * n_local) * 2
+    sets = max(1, math.ceil(ROTATION_BYTES / per_set)) if per_set < ROTATION_BYTES else 1
+    return {"workload": f"rmsnorm_gemm_bf16_{m}x{k}_to_{n}", "m": m, "k": k, "n": n,
+            "n_per_gpu": n_local, "eps": cfg["eps"],
+            "partition": "N-split, x replicated, no collective",
+            "l2": "inputs > L2" if sets == 1 else f"rotating {sets} x/C sets",
+            "params": params_for("gemm")}
+
+
+CONFIGS = {
+    "rmsnorm": rmsnorm_config,
+    "gemm8192": lambda w: gemm_config(8192, "bf16", True, w),
+    "gemm2048": lambda w: gemm_config(2048, "bf16", False, w),
+    "gemm8192_fp16": lambda w: gemm_config(8192, "fp16", True, w),
+    "gemm2048_fp16": lambda w: gemm_config(2048, "fp16", False, w),
+    "moe_small": moe_small_config,
+    "moe_large": moe_large_config,
+    "rmsnorm_gemm": rmsnorm_gemm_config,
+}
+SCALING = {"rmsnorm": "weak", "gemm2048": "weak", "gemm2048_fp16": "weak", "moe_small": "weak",
+           "gemm8192": "strong", "gemm8192_fp16": "strong", "moe_large": "strong",
+           "rmsnorm_gemm": "strong"}
+
+
 # ----------------------------------------------------------------------------- workloads
 class Rmsnorm:
     name = "rmsnorm"
@@ -204,25 +399,23 @@ class Rmsnorm:
     dtype = "bf16"
     kernel = "rmsnorm_vec_kernel<bf16,4>"
     bound = "hbm"
+    launches_per_step = 1
 
     def __init__(self, device, rank, world):
         import torch
 
         from flashattentionanycard_b200 import workloads
-        from flashattentionanycard_b200.configs.search_spaces import default_params
 
         cfg = workloads.RMSNORM
         self.m, self.n, self.eps = cfg["m"], cfg["n"], cfg["eps"]
-        self.params = default_params("rmsnorm")
+        self.params = params_for("rmsnorm")
         self.bytes_per_step = 2 * self.m * self.n * 2 + self.n * 2  # x in + y out + w
         # Rank r owns rows [r*m, (r+1)*m) of a (world*m)-row matrix: distinct seed per shard.
         x, w = workloads.rmsnorm_inputs(self.m, self.n, "bf16", seed=rank, device=device)
-        per_set = 2 * x.numel() * 2
-        self.sets = max(2, math.ceil(ROTATION_BYTES / per_set))
+        self.sets = max(2, math.ceil(ROTATION_BYTES / (2 * x.numel() * 2)))
         self.x = [x] + [x.roll(i, 0).contiguous() for i in range(1, self.sets)]
         self.y = [torch.empty_like(x) for _ in range(self.sets)]
         self.w = w
-        self.units = f"{self.m}x{self.n} rows x hidden per rank"
 
     def step(self, i):
         from flashattentionanycard_b200.kernels import rmsnorm
@@ -230,17 +423,19 @@ class Rmsnorm:
         s = i % self.sets
         rmsnorm.launch(self.x[s], self.w, self.y[s], self.params, self.eps)
 
-    launches_per_step = 1
-
-    def config(self, world):
-        return {"workload": f"rmsnorm_bf16_{self.m}x{self.n}_eps1e-6",
-                "rows_per_gpu": self.m, "hidden": self.n, "total_rows": self.m * world,
-                "partition": "row-split, no collective", "l2": f"rotating {self.sets} buffer sets "
-                f"({self.sets * 2 * self.m * self.n * 2 / 2**20:.0f} MiB > L2)",
-                "params": self.params}
-
     def value(self, seconds_per_step, world):
         return self.bytes_per_step * world / seconds_per_step / 1e9
+
+    def parity(self):
+        import torch
+
+        s = 1 % self.sets
+        rows = sample_rows(self.m, 16)
+        x = self.x[s][rows].float()
+        ref = x * torch.rsqrt(x.square().mean(-1, keepdim=True) + self.eps) * self.w.float()
+        out = gate_check(self.y[s][rows], ref, "bf16")
+        out["checked"] = f"{len(rows)} sampled rows x {self.n} columns"
+        return out
 
     # e2e through the public API with host buffers
     def e2e_setup(self):
@@ -259,30 +454,6 @@ class Rmsnorm:
         x, w = self.d_in[b]
         rmsnorm.launch(x, w, self.d_out[b], self.params, self.eps)
 
-    # CPU reference (oracle port): fp32 RMSNorm over row blocks on all host threads
-    def cpu_setup(self):
-        import numpy as np
-
-        from flashattentionanycard_b200 import workloads
-
-        x, w = workloads.rmsnorm_inputs(self.m, self.n, "bf16", seed=0)
-        self.cx = x.float().numpy()
-        self.cw = w.float().numpy()
-        self.cout = np.empty_like(self.cx)
-
-    def cpu_step(self, pool, threads):
-        from oracle import numerics
-
-        rows = self.m
-        chunk = max(1, -(-rows // threads))
-
-        def work(lo):
-            hi = min(rows, lo + chunk)
-            self.cout[lo:hi] = numerics.rmsnorm_fp32(self.cx[lo:hi], self.cw, self.eps)
-
-        list(pool.map(work, range(0, rows, chunk)))
-        return self.bytes_per_step
-
 
 class Gemm:
     unit = "TFLOP/s"
@@ -293,13 +464,13 @@ class Gemm:
         import torch
 
         from flashattentionanycard_b200 import workloads
-        from flashattentionanycard_b200.configs.search_spaces import default_params
 
         self.name = f"gemm{size}" + ("_fp16" if dtype == "fp16" else "")
         self.dtype = dtype
         self.size = size
-        self.params = default_params("gemm")
-        self.kernel = (f"gemm_tc2_kernel<{self.params['BLOCK_N']}>" if self.params.get("CTA_GROUP") == 2
+        self.params = params_for("gemm")
+        self.kernel = (f"gemm_tc2_kernel<{self.params['BLOCK_N']}>"
+                       if self.params.get("CTA_GROUP") == 2
                        else f"gemm_tc_kernel<{self.params['BLOCK_N']},dense>")
         n_local = size // world if split else size
         if split and size % world:
@@ -310,8 +481,7 @@ class Gemm:
         self.a, self.b = a, b
         self.n_local = n_local
         self.flops_per_step = 2.0 * size * size * n_local
-        per_set = (a.numel() + b.numel() + size * n_local) * 2
-        self.sets = max(1, math.ceil(ROTATION_BYTES / per_set)) if per_set < ROTATION_BYTES else 1
+        self.sets = gemm_sets(size, n_local)
         self.A = [a] + [a.roll(i, 0).contiguous() for i in range(1, self.sets)]
         self.C = [torch.empty(size, n_local, device=device, dtype=a.dtype) for _ in range(self.sets)]
         self.split = split
@@ -322,16 +492,16 @@ class Gemm:
         s = i % self.sets
         gemm.launch(self.A[s], self.b, self.C[s], self.params)
 
-    def config(self, world):
-        return {"workload": f"gemm_{self.dtype}_{self.size}^3", "m": self.size, "k": self.size,
-                "n": self.size, "n_per_gpu": self.n_local,
-                "partition": "N-split, A replicated, no collective" if self.split else "replicas",
-                "l2": "inputs > L2" if self.sets == 1 else f"rotating {self.sets} A/C sets",
-                "params": self.params}
-
     def value(self, seconds_per_step, world):
-        total = self.flops_per_step * (world if not self.split else world)
-        return total / seconds_per_step / 1e12
+        return self.flops_per_step * world / seconds_per_step / 1e12
+
+    def parity(self):
+        s = 1 % self.sets
+        rows = sample_rows(self.size, 16)
+        ref = self.A[s][rows].float() @ self.b.float()
+        out = gate_check(self.C[s][rows], ref, self.dtype)
+        out["checked"] = f"{len(rows)} sampled rows x {self.n_local} columns of this rank's C"
+        return out
 
     def e2e_setup(self):
         import torch
@@ -351,26 +521,11 @@ class Gemm:
         a, bb = self.d_in[b]
         gemm.launch(a, bb, self.d_out[b], self.params)
 
-    def cpu_setup(self):
-        from flashattentionanycard_b200 import workloads
-
-        rows = 256 if self.size > 2048 else self.size
-        a, b = workloads.gemm_inputs(self.size, self.size, self.size, self.dtype, seed=0)
-        self.ca = a[:rows].float().numpy()
-        self.cb = b[:, : self.n_local].float().numpy()
-        self.cpu_rows = rows
-
-    def cpu_step(self, pool, threads):
-        from oracle import numerics
-
-        numerics.gemm_fp32(self.ca, self.cb)  # BLAS threads
-        return 2.0 * self.cpu_rows * self.size * self.n_local
-
 
 class RmsnormGemm:
     """RMSNorm of x [4096, 4096] fused into the 4096 -> 14336 projection that
-    follows it (one kernel: norm-in-prologue tcgen05 GEMM); N split across
-    ranks with x replicated (no collective)."""
+    follows it (row-scale pass + row-scaled tcgen05 GEMM with the norm weight
+    folded into B); N split across ranks with x replicated (no collective)."""
 
     name = "rmsnorm_gemm"
     unit = "TFLOP/s"
@@ -382,19 +537,17 @@ class RmsnormGemm:
         import torch
 
         from flashattentionanycard_b200 import workloads
-        from flashattentionanycard_b200.configs.search_spaces import default_params
+        from flashattentionanycard_b200.kernels import rmsnorm_gemm
 
         cfg = workloads.RMSNORM_GEMM
         self.m, self.k, self.n, self.eps = cfg["m"], cfg["k"], cfg["n"], cfg["eps"]
         if self.n % world:
             raise SystemExit("N must divide evenly across ranks")
         self.n_local = self.n // world
-        self.params = default_params("gemm")
-        self.norm_params = default_params("rmsnorm")
+        self.params = params_for("gemm")
+        self.norm_params = params_for("rmsnorm")
         self.kernel = ("gemm_tc2_kernel<256,rowscale>" if self.params.get("CTA_GROUP") == 2
                        else "gemm_tc_kernel<256,rowscale>")
-        from flashattentionanycard_b200.kernels import rmsnorm_gemm
-
         x, w, b = workloads.rmsnorm_gemm_inputs(self.m, self.k, self.n, "bf16", seed=0,
                                                 device=device)
         self.x, self.w = x, w
@@ -433,15 +586,21 @@ class RmsnormGemm:
         rmsnorm.launch(self.X[s], self.w, self.xn, self.norm_params, self.eps)
         gemm.launch(self.xn, self.b, self.C[s], self.params)
 
-    def config(self, world):
-        return {"workload": f"rmsnorm_gemm_bf16_{self.m}x{self.k}_to_{self.n}", "m": self.m,
-                "k": self.k, "n": self.n, "n_per_gpu": self.n_local, "eps": self.eps,
-                "partition": "N-split, x replicated, no collective",
-                "l2": "inputs > L2" if self.sets == 1 else f"rotating {self.sets} x/C sets",
-                "params": self.params}
-
     def value(self, seconds_per_step, world):
         return self.flops_per_step * world / seconds_per_step / 1e12
+
+    def parity(self):
+        import torch
+
+        s = 0
+        self.step(s)  # C[0] from the fused path (the unfused comparison rewrote it)
+        torch.cuda.synchronize()
+        rows = sample_rows(self.m, 16)
+        x = self.X[s][rows].float()
+        xn = x * torch.rsqrt(x.square().mean(-1, keepdim=True) + self.eps) * self.w.float()
+        out = gate_check(self.C[s][rows], xn @ self.b.float(), "bf16")
+        out["checked"] = f"{len(rows)} sampled rows x {self.n_local} columns vs the fp32 chain"
+        return out
 
     def e2e_setup(self):
         import torch
@@ -464,21 +623,6 @@ class RmsnormGemm:
         (x,) = self.d_in[b]
         rmsnorm_gemm.launch(x, self.b_folded, self.d_out[b], self.params, self.eps)
 
-    def cpu_setup(self):
-        from flashattentionanycard_b200 import workloads
-
-        self.cpu_rows = 256
-        x, w, b = workloads.rmsnorm_gemm_inputs(self.m, self.k, self.n, "bf16", seed=0)
-        self.cx = x[: self.cpu_rows].float().numpy()
-        self.cw = w.float().numpy()
-        self.cb = b[:, : self.n_local].float().numpy()
-
-    def cpu_step(self, pool, threads):
-        from oracle import numerics
-
-        numerics.gemm_fp32(numerics.rmsnorm_fp32(self.cx, self.cw, self.eps), self.cb)
-        return 2.0 * self.cpu_rows * self.k * self.n_local
-
 
 def grouped_kernel_label(params):
     """(kernel, launches) of one grouped GEMM call with ``params``."""
@@ -486,6 +630,23 @@ def grouped_kernel_label(params):
     if params.get("CTA_GROUP", 1) == 2:
         return f"gemm_tc2_kernel<{bn},grouped>", 1
     return f"gemm_tc_kernel<{bn},grouped>", 1
+
+
+def grouped_parity(x, w, offsets, y, rows, dtype="bf16", cols=None):
+    """Gate of sampled packed rows of a grouped GEMM output y (expert of a row
+    from ``offsets``) against x[row] @ w[expert] in fp32 on the device."""
+    import bisect
+
+    import torch
+
+    offs = [int(v) for v in offsets.cpu().tolist()]
+    outs, refs = [], []
+    for r in rows:
+        e = bisect.bisect_right(offs, r) - 1
+        wm = w[e] if cols is None else w[e][:, cols]
+        refs.append(x[r:r + 1].float() @ wm.float())
+        outs.append(y[r:r + 1] if cols is None else y[r:r + 1, cols])
+    return gate_check(torch.cat(outs), torch.cat(refs), dtype)
 
 
 class MoeSmall:
@@ -498,14 +659,11 @@ class MoeSmall:
         import torch
 
         from flashattentionanycard_b200 import workloads
-        from flashattentionanycard_b200.configs.search_spaces import default_params
 
         counts = workloads.MOE_SMALL_COUNTS
         cfg = workloads.MOE_SMALL
         self.k, self.n = cfg["k"], cfg["n"]
-        # Tuned for this single-wave problem (120 tiles of 128 rows on 148 SMs):
-        # single-CTA tiles.
-        self.params = dict(default_params("moe_grouped_gemm"), CTA_GROUP=1, num_stages=4)
+        self.params = moe_small_params()
         self.kernel, self.launches_per_step = grouped_kernel_label(self.params)
         x, w = workloads.moe_inputs(counts, self.k, self.n, "bf16", seed=rank, device=device)
         self.offsets = torch.tensor(workloads.offsets_from_counts(counts), dtype=torch.int32,
@@ -514,12 +672,12 @@ class MoeSmall:
         self.flops_per_step = 2.0 * t * self.k * self.n
         nonempty = sum(1 for c in counts if c)
         self.bytes_per_step = (t * self.k + nonempty * self.k * self.n + t * self.n) * 2
-        per_set = self.bytes_per_step
-        self.sets = max(2, math.ceil(ROTATION_BYTES / per_set))
+        self.sets = max(2, math.ceil(ROTATION_BYTES / self.bytes_per_step))
         self.X = [x] + [x.roll(i, 0).contiguous() for i in range(1, self.sets)]
         self.W = [w] + [w.roll(i, 1).contiguous() for i in range(1, self.sets)]
         self.Y = [torch.empty(t, self.n, device=device, dtype=x.dtype) for _ in range(self.sets)]
         self.counts = counts
+        self.t = t
         self.sm = torch.cuda.get_device_properties(device).multi_processor_count
 
     def dominant_kernel(self, i):
@@ -532,13 +690,15 @@ class MoeSmall:
         s = i % self.sets
         moe_grouped_gemm.launch(self.X[s], self.W[s], self.offsets, self.Y[s], self.params, self.sm)
 
-    def config(self, world):
-        return {"workload": "moe_grouped_gemm_bf16_E8_K1024_N2048_T1528",
-                "expert_tokens": list(self.counts), "partition": "replicas",
-                "l2": f"rotating {self.sets} X/W/Y sets", "params": self.params}
-
     def value(self, seconds_per_step, world):
         return self.flops_per_step * world / seconds_per_step / 1e12
+
+    def parity(self):
+        s = 1 % self.sets
+        rows = sample_rows(self.t, 24)
+        out = grouped_parity(self.X[s], self.W[s], self.offsets, self.Y[s], rows)
+        out["checked"] = f"{len(rows)} sampled packed rows x {self.n} columns"
+        return out
 
     def e2e_setup(self):
         import torch
@@ -557,19 +717,6 @@ class MoeSmall:
         x, w = self.d_in[b]
         moe_grouped_gemm.launch(x, w, self.offsets, self.d_out[b], self.params, self.sm)
 
-    def cpu_setup(self):
-        from flashattentionanycard_b200 import workloads
-
-        x, w = workloads.moe_inputs(self.counts, self.k, self.n, "bf16", seed=0)
-        self.cx, self.cw = x.float().numpy(), w.float().numpy()
-        self.cstarts = workloads.offsets_from_counts(self.counts)
-
-    def cpu_step(self, pool, threads):
-        from oracle import numerics
-
-        numerics.grouped_gemm_fp32(self.cx, self.cw, self.cstarts)
-        return self.flops_per_step
-
 
 class MoeLarge:
     name = "moe_large"
@@ -581,21 +728,21 @@ class MoeLarge:
         import torch
 
         from flashattentionanycard_b200 import workloads
-        from flashattentionanycard_b200.configs.search_spaces import default_params
         from flashattentionanycard_b200.kernels.moe_routing import MoeRouter
 
-        cfg = dict(workloads.MOE_LARGE)
-        cfg["experts"] = MOE_EXPERTS or cfg["experts"]
+        cfg = moe_large_cfg()
         self.cfg = cfg
         self.world, self.rank = world, rank
-        self.params = default_params("moe_grouped_gemm")
+        self.params = params_for("moe_grouped_gemm")
         self.kernel, gemm_launches = grouped_kernel_label(self.params)
         self.launches_per_step = 4 + gemm_launches  # route: count, scan, scatter; gather; GEMM
         self.x, self.w, ids = workloads.moe_large_inputs("bf16", seed=0, device=device,
                                                          experts=cfg["experts"])
+        self.ids_cpu = ids
         self.sm = torch.cuda.get_device_properties(device).multi_processor_count
         a = ids.numel()
         self.flops_per_step = 2.0 * a * cfg["k"] * cfg["n"]  # whole job, all ranks
+        self.graphable = True
         if world > 1:
             self._init_expert_parallel(ids, device)
             return
@@ -606,6 +753,7 @@ class MoeLarge:
 
     def _init_expert_parallel(self, ids, device):
         import numpy as np
+        import torch
         import torch.distributed as dist
 
         from flashattentionanycard_b200 import expert_parallel as ep
@@ -613,14 +761,17 @@ class MoeLarge:
         cfg, world, rank = self.cfg, self.world, self.rank
         flat = ids.reshape(-1).numpy()
         tpr = cfg["tokens"] // world
-        self.placement = ep.plan_placement(np.bincount(flat, minlength=cfg["experts"]), world)
+        _, self.placement = moe_large_placement(cfg, world)
         self.plan = ep.plan_splits(flat, self.placement, cfg["topk"], tpr)
         local = self.w[ep.local_weight_slices(self.placement, rank)].contiguous()
+        # Columns kept for the parity check after the full weights are dropped.
+        self.check_cols = list(range(256)) + list(range(cfg["n"] - 256, cfg["n"]))
+        self.w_cols = self.w[:, :, self.check_cols].contiguous()
         del self.w  # each rank keeps only its virtual experts' weights
         self.x_local = self.x[rank * tpr:(rank + 1) * tpr].contiguous()
         del self.x
         self.ids_local = ids.reshape(-1)[rank * tpr * cfg["topk"]:(rank + 1) * tpr * cfg["topk"]]
-        self.ids_local = self.ids_local.to(torch_int32()).to(device)
+        self.ids_local = self.ids_local.to(torch.int32).to(device)
         self.comm = EP_COMM
         if self.comm == "peer":
             self.ep = ep.PeerExpertParallelMoE(local, self.placement, self.plan, rank, world,
@@ -636,15 +787,13 @@ class MoeLarge:
                                            params=self.params, sm_count=self.sm)
             # routing/keys/sorts/checks + 4 gathers + grouped GEMM
             self.launches_per_step = 20 + grouped_kernel_label(self.params)[1]
-        import torch
-
         torch.cuda.empty_cache()
-        # Collectives between kernels: timed eagerly.  (Capturing the peer
-        # path's steps, NCCL collectives included, in CUDA graphs hung a 2-GPU
-        # run until its outer timeout; the cause was not found.)
+        # Collectives between kernels: timed eagerly.
         self.graphable = False
         rows = int(self.placement.rank_rows[rank])
         self.kernel_flops = 2.0 * rows * cfg["k"] * cfg["n"]
+        self.expected_counts = np.bincount(flat, minlength=cfg["experts"]).astype(np.int32)
+        self.expected_local_rows = np.asarray(self.plan.local_rows[rank], dtype=np.int64)
 
     def step(self, i):
         from flashattentionanycard_b200.kernels import moe_grouped_gemm
@@ -658,30 +807,71 @@ class MoeLarge:
         moe_grouped_gemm.launch(self.packed, self.w, self.router.offsets, self.y, self.params,
                                 self.sm)
 
-    def config(self, world):
-        c = self.cfg
-        out = {"workload": f"moe_bf16_E{c['experts']}_K{c['k']}_N{c['n']}_T{c['tokens']}_top2_zipf1.1",
-               "partition": "single GPU (all experts local)",
-               "step": "route + gather + grouped GEMM", "l2": "W 7.5 GB > L2",
-               "params": self.params}
-        if world > 1:
-            p = self.placement
-            step = ("all-gather ids + route + NVLink peer-store dispatch + grouped GEMM with "
-                    "peer-store combine epilogue, one-word all-reduce barriers, eager"
-                    if self.comm == "peer" else
-                    "all-gather ids + route + dispatch all-to-all + grouped GEMM + "
-                    "combine all-to-all (NCCL), eager")
-            out.update({
-                "partition": f"expert-parallel over {world} GPUs: {p.virtual_experts} virtual "
-                             f"experts (hot experts replicated, rows split), LPT placement",
-                "step": step, "ep_comm": self.comm,
-                "rows_per_rank": [int(v) for v in p.rank_rows],
-                "max_replicas": int(p.replicas.max()),
-            })
-        return out
+    def dominant_kernel(self, i):  # noqa: ARG002 - same inputs every launch
+        from flashattentionanycard_b200.kernels import moe_grouped_gemm
+
+        if self.world > 1:
+            if self.comm == "peer":
+                self.ep.compute_and_combine()
+            else:
+                self.ep.compute()
+            return
+        moe_grouped_gemm.launch(self.packed, self.w, self.router.offsets, self.y, self.params,
+                                self.sm)
 
     def value(self, seconds_per_step, world):
         return self.flops_per_step / seconds_per_step / 1e12  # whole job at any world size
+
+    def parity(self):
+        import numpy as np
+        import torch
+
+        topk = self.cfg["topk"]
+        if self.world == 1:
+            self.step(0)
+            torch.cuda.synchronize()
+            flat = self.ids_cpu.reshape(-1).numpy()
+            exact = bool(np.array_equal(self.router.counts.cpu().numpy(),
+                                        np.bincount(flat, minlength=self.cfg["experts"])))
+            exact = exact and bool(np.array_equal(self.router.perm.cpu().numpy(),
+                                                  np.argsort(flat, kind="stable")))
+            rows = sample_rows(self.y.shape[0], 32)
+            perm = self.router.perm.cpu()
+            x_rows = self.x[(perm[rows] // topk).to(self.x.device)]
+            xs = torch.zeros_like(self.packed)
+            xs[rows] = x_rows
+            out = grouped_parity(xs, self.w, self.router.offsets, self.y, rows)
+            out["ok"] = out["ok"] and exact
+            out["routing_counts_exact"] = exact
+            out["checked"] = (f"{len(rows)} sampled packed rows x {self.cfg['n']} columns; "
+                              "expert counts and the permutation bit-exact vs numpy "
+                              "bincount / stable argsort")
+            return out
+        self.step(0)
+        torch.cuda.synchronize()
+        ep = self.ep
+        route = ep.route_global if hasattr(ep, "route_global") else None
+        exact = route is not None and bool(np.array_equal(route.counts.cpu().numpy(),
+                                                           self.expected_counts))
+        if self.comm == "peer":
+            lrows = np.diff(ep.loffs.cpu().numpy().astype(np.int64))
+            exact = exact and bool(np.array_equal(lrows, self.expected_local_rows))
+        out_rows = ep.out
+        rows = sample_rows(out_rows.shape[0], 32, seed=self.rank)
+        ids = self.ids_local.reshape(-1).cpu()
+        cols = self.check_cols
+        refs, outs = [], []
+        for r in rows:
+            e = int(ids[r])
+            refs.append(self.x_local[r // topk:r // topk + 1].float() @ self.w_cols[e].float())
+            outs.append(out_rows[r:r + 1, cols])
+        res = gate_check(torch.cat(outs), torch.cat(refs), "bf16")
+        res["ok"] = res["ok"] and exact
+        res["plan_counts_exact"] = exact
+        res["checked"] = (f"rank {self.rank}: {len(rows)} sampled output rows x {len(cols)} "
+                          "columns (first and last 256); global expert counts and local rows "
+                          "per virtual expert bit-exact vs the host plan")
+        return res
 
     def e2e_setup(self):
         import torch
@@ -718,20 +908,10 @@ class MoeLarge:
         moe_grouped_gemm.launch(self.packed, self.w, self.router.offsets, self.d_out[b],
                                 self.params, self.sm)
 
-    def cpu_setup(self):
-        import numpy as np
-
-        c = self.cfg
-        self.cx = self.x[:256].float().cpu().numpy()
-        self.cw = self.w[0].float().cpu().numpy()
-        self.cpu_flops = 2.0 * 256 * c["k"] * c["n"]
-        self._np = np
-
-    def cpu_step(self, pool, threads):
-        from oracle import numerics
-
-        numerics.gemm_fp32(self.cx, self.cw)
-        return self.cpu_flops
+    def release(self):
+        """Unmap the peers' buffers (every rank, after a barrier)."""
+        if self.world > 1 and hasattr(self.ep, "close"):
+            self.ep.close()
 
 
 WORKLOADS = {
@@ -750,37 +930,142 @@ DEFAULT_STEPS = {"rmsnorm": 4000, "gemm8192": 200, "gemm2048": 2000, "gemm8192_f
 
 
 # ----------------------------------------------------------------------------- CPU reference
-def cpu_measure(workload, seconds, min_reps=3):
-    """Time the oracle port of the workload on the host cores for ~``seconds``."""
-    import numpy as np
+class CpuLeg:
+    """The reference's FP32 CPU path (oracle port, numpy/BLAS) of one workload,
+    on a bounded sample; ``step`` returns the work done (bytes or FLOPs)."""
 
+    def __init__(self, name):
+        from flashattentionanycard_b200 import workloads
+
+        self.name = name
+        self.unit = "GB/s" if name == "rmsnorm" else "TFLOP/s"
+        if name == "rmsnorm":
+            cfg = workloads.RMSNORM
+            m, n, eps = cfg["m"], cfg["n"], cfg["eps"]
+            x, w = workloads.rmsnorm_inputs(m, n, "bf16", seed=0)
+            self.cx, self.cw, self.eps = x.float().numpy(), w.float().numpy(), eps
+            self.sample = "numpy fp32 RMSNorm of the full 4096x4096 input, rows split over host threads"
+            self.work = 2 * m * n * 2 + n * 2
+        elif name.startswith("gemm"):
+            size = 8192 if name.startswith("gemm8192") else 2048
+            dtype = "fp16" if name.endswith("_fp16") else "bf16"
+            rows = 256 if size > 2048 else size
+            a, b = workloads.gemm_inputs(size, size, size, dtype, seed=0)
+            self.ca, self.cb = a[:rows].float().numpy(), b.float().numpy()
+            self.sample = f"numpy/BLAS fp32 GEMM of {rows} rows of A x B (K={size}, N={size})"
+            self.work = 2.0 * rows * size * size
+        elif name == "moe_small":
+            counts = workloads.MOE_SMALL_COUNTS
+            k, n = workloads.MOE_SMALL["k"], workloads.MOE_SMALL["n"]
+            x, w = workloads.moe_inputs(counts, k, n, "bf16", seed=0)
+            self.cx, self.cw = x.float().numpy(), w.float().numpy()
+            self.cstarts = workloads.offsets_from_counts(counts)
+            self.sample = "numpy/BLAS fp32 per-expert GEMMs of the full 8-expert problem"
+            self.work = 2.0 * sum(counts) * k * n
+        elif name == "rmsnorm_gemm":
+            cfg = workloads.RMSNORM_GEMM
+            rows = 256
+            x, w, b = workloads.rmsnorm_gemm_inputs(cfg["m"], cfg["k"], cfg["n"], "bf16", seed=0)
+            self.cx, self.cw, self.cb = (x[:rows].float().numpy(), w.float().numpy(),
+                                         b.float().numpy())
+            self.eps = cfg["eps"]
+            self.sample = (f"numpy fp32 RMSNorm of {rows} rows of x, then BLAS fp32 GEMM with B "
+                           f"(K={cfg['k']}, N={cfg['n']})")
+            self.work = 2.0 * rows * cfg["k"] * cfg["n"]
+        elif name == "moe_large":
+            import torch
+
+            cfg = workloads.MOE_LARGE
+            g = torch.Generator().manual_seed(0)
+            self.cx = torch.randn(256, cfg["k"], generator=g).bfloat16().float().numpy()
+            self.cw = (0.02 * torch.randn(cfg["k"], cfg["n"], generator=g)).bfloat16().float().numpy()
+            self.sample = "numpy/BLAS fp32 GEMM of 256 tokens x one expert's W[4096, 14336]"
+            self.work = 2.0 * 256 * cfg["k"] * cfg["n"]
+        else:
+            raise ValueError(name)
+
+    def step(self, pool, threads):
+        from oracle import numerics
+
+        if self.name == "rmsnorm":
+            rows = self.cx.shape[0]
+            chunk = max(1, -(-rows // threads))
+            out = getattr(self, "cout", None)
+            if out is None:
+                import numpy as np
+
+                out = self.cout = np.empty_like(self.cx)
+
+            def work(lo):
+                hi = min(rows, lo + chunk)
+                out[lo:hi] = numerics.rmsnorm_fp32(self.cx[lo:hi], self.cw, self.eps)
+
+            list(pool.map(work, range(0, rows, chunk)))
+        elif self.name.startswith("gemm") or self.name == "moe_large":
+            numerics.gemm_fp32(self.ca if hasattr(self, "ca") else self.cx,
+                               self.cb if hasattr(self, "cb") else self.cw)
+        elif self.name == "moe_small":
+            numerics.grouped_gemm_fp32(self.cx, self.cw, self.cstarts)
+        elif self.name == "rmsnorm_gemm":
+            numerics.gemm_fp32(numerics.rmsnorm_fp32(self.cx, self.cw, self.eps), self.cb)
+        return self.work
+
+
+def cpu_measure(name, seconds, min_reps=3):
+    """Time the oracle port of a workload on the host cores for ~``seconds``."""
     threads = cpu_threads()
     os.environ.setdefault("OMP_NUM_THREADS", str(threads))
-    workload.cpu_setup()
+    leg = CpuLeg(name)
     with ThreadPoolExecutor(threads) as pool:
-        workload.cpu_step(pool, threads)  # warm
+        leg.step(pool, threads)  # warm
         reps, work, t0 = 0, 0.0, time.perf_counter()
         while reps < min_reps or time.perf_counter() - t0 < seconds:
-            work += workload.cpu_step(pool, threads)
+            work += leg.step(pool, threads)
             reps += 1
         elapsed = time.perf_counter() - t0
-    del np
-    scale = 1e9 if workload.unit == "GB/s" else 1e12
-    return work / elapsed / scale, reps, elapsed, threads
+    scale = 1e9 if leg.unit == "GB/s" else 1e12
+    return {"value": work / elapsed / scale, "unit": leg.unit, "cores": threads, "kind": "port",
+            "sample": f"{leg.sample}; {reps} reps in {elapsed:.1f} s"}
 
 
-def cpu_sample_description(workload):
-    if workload.name == "rmsnorm":
-        return "numpy fp32 RMSNorm of the full 4096x4096 input, rows split over host threads"
-    if workload.name.startswith("gemm"):
-        return (f"numpy/BLAS fp32 GEMM of {workload.cpu_rows} rows of A x B[:, :{workload.n_local}]"
-                f" (K={workload.size})")
-    if workload.name == "moe_small":
-        return "numpy/BLAS fp32 per-expert GEMMs of the full 8-expert problem"
-    if workload.name == "rmsnorm_gemm":
-        return (f"numpy fp32 RMSNorm of {workload.cpu_rows} rows of x, then BLAS fp32 GEMM with "
-                f"B[:, :{workload.n_local}] (K={workload.k})")
-    return "numpy/BLAS fp32 GEMM of 256 tokens x one expert's W[4096, 14336]"
+def secondary_names(args):
+    if args.secondary == "none":
+        return []
+    if args.secondary == "auto":
+        return list(SECONDARY_AUTO) if args.workload == "rmsnorm" else []
+    names = [s for s in args.secondary.split(",") if s]
+    for s in names:
+        if s not in WORKLOADS:
+            raise SystemExit(f"unknown secondary workload {s!r}")
+    return [s for s in names if s != args.workload]
+
+
+def reference_entry(name, args, world):
+    """One workload of the --impl reference arm: K bounded CPU steps after W untimed ones."""
+    import torch
+
+    torch.set_num_threads(cpu_threads())
+    threads = cpu_threads()
+    leg = CpuLeg(name)
+    times, work = [], 0.0
+    with ThreadPoolExecutor(threads) as pool:
+        for _ in range(args.warmup):
+            leg.step(pool, threads)
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            work += leg.step(pool, threads)
+            times.append(time.perf_counter() - t0)
+    total = sum(times)
+    scale = 1e9 if leg.unit == "GB/s" else 1e12
+    value = work / total / scale
+    return {
+        "workload": name, "value": value, "unit": leg.unit, "ms_per_step": 1e3 * total / args.steps,
+        "steps": args.steps, "higher_is_better": True, "scaling": SCALING[name],
+        "dtype": "f32", "config": CONFIGS[name](world),
+        "cpu_baseline": {"value": value, "unit": leg.unit, "cores": threads, "kind": "port",
+                         "sample": leg.sample},
+        "e2e": {"value": value, "unit": leg.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
 
 
 def run_reference(args):
@@ -788,102 +1073,21 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    import torch
-
-    torch.set_num_threads(cpu_threads())
-    wl = WORKLOADS[args.workload]
-    device = "cpu"
-    # Build the workload description without a GPU: only the CPU legs are used.
-    workload = _cpu_only_workload(args.workload)
-    times = []
-    work = 0.0
-    threads = cpu_threads()
-    workload.cpu_setup()
-    with ThreadPoolExecutor(threads) as pool:
-        for _ in range(args.warmup):
-            workload.cpu_step(pool, threads)
-        for _ in range(args.steps):
-            t0 = time.perf_counter()
-            work += workload.cpu_step(pool, threads)
-            times.append(time.perf_counter() - t0)
-    total = sum(times)
-    scale = 1e9 if workload.unit == "GB/s" else 1e12
-    value = work / total / scale
-    del wl, device
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    head = reference_entry(args.workload, args, world)
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": workload.unit,
+        "impl": "reference", "metric": METRIC, "value": head["value"], "unit": head["unit"],
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": workload.cpu_config(),
-        "cpu_baseline": {"value": value, "unit": workload.unit, "cores": threads,
-                         "kind": "port", "sample": cpu_sample_description(workload)},
-        "e2e": {"value": value, "unit": workload.unit, "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
+        "ms_per_step": head["ms_per_step"], "higher_is_better": True,
+        "scaling": head["scaling"], "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded inputs of the benchmark configuration shapes)",
+        "config": head["config"], "cpu_baseline": head["cpu_baseline"], "e2e": head["e2e"],
     }
+    secondary = [reference_entry(name, args, world) for name in secondary_names(args)]
+    if secondary:
+        line["secondary"] = secondary
     print(json.dumps(line))
     return 0
-
-
-def _cpu_only_workload(name):
-    """A workload object whose CPU legs run without touching a GPU."""
-    from flashattentionanycard_b200 import workloads
-
-    class CpuOnly:
-        pass
-
-    if name == "rmsnorm":
-        w = Rmsnorm.__new__(Rmsnorm)
-        cfg = workloads.RMSNORM
-        w.m, w.n, w.eps = cfg["m"], cfg["n"], cfg["eps"]
-        w.bytes_per_step = 2 * w.m * w.n * 2 + w.n * 2
-        w.cpu_config = lambda: {"workload": f"rmsnorm_bf16_{w.m}x{w.n}_eps1e-6",
-                                "sample": "full 4096x4096 per step"}
-        return w
-    if name.startswith("gemm") and not name.startswith("gemm_"):
-        w = Gemm.__new__(Gemm)
-        w.size = 8192 if name.startswith("gemm8192") else 2048
-        w.dtype = "fp16" if name.endswith("_fp16") else "bf16"
-        w.name, w.n_local = name, w.size
-        w.cpu_config = lambda: {"workload": f"gemm_{w.dtype}_{w.size}^3",
-                                "sample": f"{256 if w.size > 2048 else w.size} rows of A per step"}
-        return w
-    if name == "moe_small":
-        w = MoeSmall.__new__(MoeSmall)
-        w.counts = workloads.MOE_SMALL_COUNTS
-        w.k, w.n = workloads.MOE_SMALL["k"], workloads.MOE_SMALL["n"]
-        w.flops_per_step = 2.0 * sum(w.counts) * w.k * w.n
-        w.cpu_config = lambda: {"workload": "moe_grouped_gemm_bf16_E8_K1024_N2048_T1528"}
-        return w
-    if name == "rmsnorm_gemm":
-        w = RmsnormGemm.__new__(RmsnormGemm)
-        cfg = workloads.RMSNORM_GEMM
-        w.m, w.k, w.n, w.eps = cfg["m"], cfg["k"], cfg["n"], cfg["eps"]
-        w.n_local = w.n
-        w.cpu_config = lambda: {"workload": f"rmsnorm_gemm_bf16_{w.m}x{w.k}_to_{w.n}",
-                                "sample": "256 rows of x per step"}
-        return w
-    w = CpuOnly()
-    cfg = workloads.MOE_LARGE
-    w.name, w.unit = "moe_large", "TFLOP/s"
-
-    def setup():
-        import torch
-
-        g = torch.Generator().manual_seed(0)
-        w.cx = torch.randn(256, cfg["k"], generator=g).bfloat16().float().numpy()
-        w.cw = (0.02 * torch.randn(cfg["k"], cfg["n"], generator=g)).bfloat16().float().numpy()
-
-    def step(pool, threads):
-        from oracle import numerics
-
-        numerics.gemm_fp32(w.cx, w.cw)
-        return 2.0 * 256 * cfg["k"] * cfg["n"]
-
-    w.cpu_setup, w.cpu_step = setup, step
-    w.cpu_config = lambda: {"workload": "moe_bf16_E64_K4096_N14336_T16384_top2_zipf1.1",
-                            "sample": "256 tokens x one expert per step"}
-    return w
 
 
 # ----------------------------------------------------------------------------- GPU arm
@@ -932,29 +1136,40 @@ def capture_steps(workload, stream, first, count):
     return graph
 
 
-def run_ours(args):
+def max_over_ranks(value, world, device):
     import torch
     import torch.distributed as dist
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world != args.gpus:
-        if world == 1 and args.gpus > 1:
-            raise SystemExit("--gpus N > 1 must be launched with torch.distributed.run")
-    device = torch.device("cuda", local)
-    torch.cuda.set_device(device)
-    if world > 1:
-        from datetime import timedelta
+    if world == 1:
+        return value
+    t = torch.tensor([value], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+
+def all_ranks_ok(ok, world, device):
+    import torch
+    import torch.distributed as dist
+
+    if world == 1:
+        return ok
+    t = torch.tensor([0 if ok else 1], device=device, dtype=torch.int32)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return int(t.item()) == 0
+
+
+def measure_workload(name, args, steps, ctx):
+    """Time one workload (K steps after W warm-up steps), its dominant kernel,
+    its end-to-end rate and its parity; returns the result dict (every rank
+    takes the same collective steps)."""
+    import torch
+    import torch.distributed as dist
 
     from flashattentionanycard_b200 import _native
 
-    _native.load()
-    peaks, peak_kind = load_peaks()
-    workload = WORKLOADS[args.workload](device, rank, world)
-    stream = torch.cuda.Stream(device)
+    world, rank, device, stream = ctx["world"], ctx["rank"], ctx["device"], ctx["stream"]
+    sampler, peaks, peak_kind = ctx["sampler"], ctx["peaks"], ctx["peak_kind"]
+    workload = WORKLOADS[name](device, rank, world)
     torch.cuda.synchronize()
 
     # warm-up (eager, outside capture: first calls set kernel attributes)
@@ -964,7 +1179,6 @@ def run_ours(args):
     stream.synchronize()
     _native.device_status(reset=True)
 
-    steps = args.steps
     graphable = getattr(workload, "graphable", True)
     graphs = []
     if graphable:
@@ -974,16 +1188,19 @@ def run_ours(args):
             count = min(chunk, steps - done)
             graphs.append(capture_steps(workload, stream, done, count))
             done += count
-        # one untimed replay of the first graph (graph upload)
-        graphs[0].replay()
+        graphs[0].replay()  # graph upload
         torch.cuda.synchronize()
 
-    sampler = ClockSampler(local)
-    sampler.start()
-    time.sleep(0.3)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    # Untimed step(s) right before the start event: the timed region starts on
+    # a busy GPU at clock, as the reference's measure() replays once first.
+    with torch.cuda.stream(stream):
+        if graphable:
+            graphs[0].replay()
+        else:
+            workload.step(0)
     begin, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0 = time.perf_counter()
     begin.record(stream)
@@ -999,34 +1216,29 @@ def run_ours(args):
     t1 = time.perf_counter()
     if world > 1:
         dist.barrier()
-    clocks = sampler.stop(t0, t1)
-    ms = begin.elapsed_time(end)
-    if world > 1:
-        t = torch.tensor([ms], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    clocks = sampler.window(t0, t1)
+    ms = max_over_ranks(begin.elapsed_time(end), world, device)
     code, detail = _native.device_status(reset=True)
     if code:
-        raise SystemExit(f"kernel reported device status {code} (detail {detail})")
+        raise SystemExit(f"{name}: kernel reported device status {code} (detail {detail})")
     del graphs
     ms_per_step = ms / steps
     value = workload.value(ms_per_step / 1e3, world)
 
     # Dominant kernel's average launch duration.  A one-kernel step: the timed
     # region itself (events around K launches).  Otherwise a graph of the
-    # dominant kernel alone, timed the same way.
+    # dominant kernel alone (eager launches for the expert-parallel kernel),
+    # timed the same way.
     if workload.launches_per_step == 1:
         kernel_ms = ms_per_step
         kernel_timing = "timed region / launches"
     else:
-        dominant = getattr(workload, "dominant_kernel", None) or (lambda i: _last_kernel(workload, i))
-        kernel_ms = graph_time_ms(stream, dominant, 20)
+        # No collectives inside the dominant kernel, so it is captured even
+        # for the (eagerly timed) expert-parallel step.
+        kernel_ms = graph_time_ms(stream, workload.dominant_kernel, 20)
         kernel_timing = "graph of 20 launches of the dominant kernel alone, best of 3"
-    if workload.bound == "hbm" and workload.unit == "GB/s":
-        achieved = workload.bytes_per_step / (kernel_ms / 1e3) / 1e9
-        peak = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
-        unit_r = "GB/s"
-    elif workload.bound == "hbm":
+    kernel_ms = max_over_ranks(kernel_ms, world, device)
+    if workload.unit == "GB/s" or workload.bound == "hbm":
         achieved = workload.bytes_per_step / (kernel_ms / 1e3) / 1e9
         peak = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
         unit_r = "GB/s"
@@ -1059,6 +1271,12 @@ def run_ours(args):
         roofline["peak_sustained"] = sustained
         roofline["frac_of_sustained"] = achieved / sustained
 
+    # Parity of this run's output (every rank checks its own part).
+    fp32_reference_mode()
+    parity = workload.parity()
+    parity["reference"] = "torch fp32 on the device (TF32 off), the reference's gate tolerances"
+    parity["ok"] = all_ranks_ok(bool(parity["ok"]), world, device)
+
     # End to end through the public API with pinned host buffers.  Every step
     # uploads its inputs and downloads its result; consecutive steps overlap
     # (upload of step i+1 while step i's result downloads: PCIe is full duplex).
@@ -1082,65 +1300,114 @@ def run_ours(args):
         ee.record(stream)
         torch.cuda.synchronize()
         e2e_ms = eb.elapsed_time(ee) / e2e_steps
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = max_over_ranks(e2e_ms, world, device)
     e2e = {"value": workload.value(e2e_ms / 1e3, world), "unit": workload.unit,
            "h2d_bytes_per_step": workload.h2d, "d2h_bytes_per_step": workload.d2h,
            "ms_per_step": e2e_ms, "steps": e2e_steps,
            "api": "flashattentionanycard_b200.kernels launch() with pinned host copies",
            "overlap": ("two streams: upload of step i+1 overlaps the download of step i"
                        if pipelined else "sequential per step")}
+    result = {
+        "workload": name, "value": value, "unit": workload.unit, "steps": steps,
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": SCALING[name],
+        "dtype": workload.dtype, "config": CONFIGS[name](world), "roofline": roofline,
+        "e2e": e2e, "clocks": clocks, "gpu_launches": steps * workload.launches_per_step,
+        "parity": parity,
+    }
+    if unfused is not None:
+        result["unfused"] = unfused
+    # Free this workload before the next one (peer mappings first, on every rank).
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    if hasattr(workload, "release"):
+        workload.release()
+    if world > 1:
+        dist.barrier()
+    del workload
+    gc.collect()
+    torch.cuda.empty_cache()
+    return result
 
-    cpu = None
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        if world == 1 and args.gpus > 1:
+            raise SystemExit("--gpus N > 1 must be launched with torch.distributed.run")
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+
+    from flashattentionanycard_b200 import _native
+
+    _native.load()
+    peaks, peak_kind = load_peaks()
+    sampler = ClockSampler(local)
+    sampler.start()  # started well before the first timed region (nvidia-smi start-up)
+    ctx = {"world": world, "rank": rank, "device": device, "stream": torch.cuda.Stream(device),
+           "sampler": sampler, "peaks": peaks, "peak_kind": peak_kind}
+    names = [args.workload] + secondary_names(args)
+    results = []
+    try:
+        for name in names:
+            steps = args.steps if args.steps is not None else DEFAULT_STEPS[name]
+            results.append(measure_workload(name, args, steps, ctx))
+    finally:
+        sampler.stop()
+
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu_workload = _cpu_only_workload(args.workload)
-        v, reps, elapsed, threads = cpu_measure(cpu_workload, args.cpu_seconds)
-        cpu = {"value": v, "unit": workload.unit, "cores": threads, "kind": "port",
-               "sample": cpu_sample_description(cpu_workload) +
-               f"; {reps} reps in {elapsed:.1f} s"}
-
+        for i, res in enumerate(results):
+            seconds = args.cpu_seconds if i == 0 else args.cpu_seconds / 2
+            res["cpu_baseline"] = cpu_measure(res["workload"], seconds)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    parity_ok = all(r["parity"]["ok"] for r in results)
     if rank != 0:
-        return 0
-    scaling = ("weak" if args.workload in ("rmsnorm", "gemm2048", "gemm2048_fp16", "moe_small")
-               else "strong")
+        return 0 if parity_ok else 1
+    head = results[0]
     line = {
-        "metric": METRIC, "value": value, "unit": workload.unit, "n_gpus": world,
-        "steps": steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-        "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
-        "dtype": workload.dtype, "data": "synthetic (seeded inputs of the benchmark configuration shapes)",
-        "config": workload.config(world), "roofline": roofline, "cpu_baseline": cpu,
-        "e2e": e2e, "clocks": clocks, "gpu_launches": steps * workload.launches_per_step,
-        "impl": "ours",
+        "metric": METRIC, "value": head["value"], "unit": head["unit"], "n_gpus": world,
+        "steps": head["steps"], "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
+        "higher_is_better": True, "scaling": head["scaling"], "vs_baseline": None,
+        "dtype": head["dtype"],
+        "data": "synthetic (seeded inputs of the benchmark configuration shapes)",
+        "config": head["config"], "roofline": head["roofline"],
+        "cpu_baseline": head.get("cpu_baseline"), "e2e": head["e2e"], "clocks": head["clocks"],
+        "gpu_launches": head["gpu_launches"], "parity": head["parity"], "impl": "ours",
     }
-    if unfused is not None:
-        line["unfused"] = unfused
+    if "unfused" in head:
+        line["unfused"] = head["unfused"]
+    if len(results) > 1:
+        line["secondary"] = results[1:]
     print(json.dumps(line))
+    if not parity_ok:
+        failed = [r["workload"] for r in results if not r["parity"]["ok"]]
+        print(f"parity check failed: {failed}", file=sys.stderr)
+        return 1
     return 0
 
 
-def torch_int32():
-    import torch
-
-    return torch.int32
-
-
-def _last_kernel(workload, i):  # noqa: ARG001 - same inputs every launch
-    from flashattentionanycard_b200.kernels import moe_grouped_gemm
-
-    if getattr(workload, "world", 1) > 1:
-        if workload.comm == "peer":
-            workload.ep.compute_and_combine()
-        else:
-            workload.ep.compute()
-        return
-
-    moe_grouped_gemm.launch(workload.packed, workload.w, workload.router.offsets, workload.y,
-                            workload.params, workload.sm)
+def parse_params(text):
+    """--params 'gemm:GROUP_M=16,num_stages=5;moe_grouped_gemm:RASTER=2'."""
+    out = {}
+    for group in filter(None, (text or "").split(";")):
+        kernel, _, body = group.partition(":")
+        entries = {}
+        for item in filter(None, body.split(",")):
+            key, _, value = item.partition("=")
+            entries[key.strip()] = int(value)
+        out[kernel.strip()] = entries
+    return out
 
 
 def main():
@@ -1150,6 +1417,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="rmsnorm")
+    ap.add_argument("--secondary", default="auto",
+                    help="'auto' (with the default rmsnorm headline: gemm8192,moe_large), "
+                         "'none', or a comma list of workloads timed in the same run")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--experts", type=int, default=None,
@@ -1157,12 +1427,15 @@ def main():
                          "same kernel, e.g. for ncu captures)")
     ap.add_argument("--ep-comm", choices=("peer", "nccl"), default="peer",
                     help="moe_large at N>1: NVLink peer stores (fused) or NCCL all-to-all")
+    ap.add_argument("--params", default="",
+                    help="launch-parameter overrides, e.g. 'gemm:GROUP_M=16;rmsnorm:num_warps=8'")
     args = ap.parse_args()
-    global EP_COMM, MOE_EXPERTS
+    global EP_COMM, MOE_EXPERTS, PARAM_OVERRIDES
     EP_COMM = args.ep_comm
     MOE_EXPERTS = args.experts
-    if args.steps is None:
-        args.steps = 20 if args.impl == "reference" else DEFAULT_STEPS[args.workload]
+    PARAM_OVERRIDES = parse_params(args.params)
+    if args.impl == "reference" and args.steps is None:
+        args.steps = 20
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
