@@ -17,6 +17,8 @@ ABI_VERSION = 1
 FP16, BF16 = 0, 1
 KERNEL_GEMM, KERNEL_RMSNORM, KERNEL_MOE_GROUPED_GEMM, KERNEL_RMSNORM_GEMM = 0, 1, 2, 3
 
+BOKT_ERR_CUDA_RC = 4
+
 ERRORS = {
     1: "invalid argument",
     2: "unsupported",
@@ -85,6 +87,13 @@ SIGNATURES = {
     "bokt_moe_grouped_gemm": (
         _I32,
         [_VP, _VP, _VP, _I32, _VP, _I32, _I32, _I32, _I32, _I32, _I32, _PP, _VP],
+    ),
+    "bokt_gemm_ex": (_I32, [_VP, _VP, _VP, _I32, _I32, _I32, _I32, _PP, _VP, _I64, _VP]),
+    "bokt_gemm_workspace_bytes": (_I64, [_I32, _PP]),
+    "bokt_splitk_schedule": (_I32, [_I32, _I32, _I32, _I32, _VP, _I32]),
+    "bokt_moe_grouped_gemm_ex": (
+        _I32,
+        [_VP, _VP, _VP, _I32, _VP, _I32, _I32, _I32, _I32, _I32, _I32, _PP, _VP, _I64, _VP],
     ),
     "bokt_moe_route_workspace_bytes": (_I64, [_I32, _I32]),
     "bokt_moe_route": (_I32, [_VP, _I32, _I32, _VP, _VP, _VP, _VP, _VP, _VP, _I64, _VP]),
@@ -206,6 +215,51 @@ class CompiledKernel:
         self.threads = int(attrs.threads)
         self.path = {0: "tcgen05", 1: "simt", 2: "vector", 3: "scalar", 4: "ring",
                      5: "pipelined"}.get(attrs.path, "?")
+
+
+_splitk_ws = {}
+
+
+def splitk_workspace(kernel, params, device):
+    """(pointer, bytes) of the split-K workspace for ``params`` on ``device``
+    ((None, 0) when SPLIT_K <= 1).
+
+    One zero-filled buffer per device, allocated on the first split-K call
+    (that first call must come before any graph capture, as the reference's
+    warm-up calls do) and kept for the life of the process; it grows only if a
+    later configuration needs more.  Calls that share it must not overlap on
+    the GPU: the library keeps a launch sequence number in it."""
+    import torch
+
+    if int((params or {}).get("SPLIT_K", 1)) <= 1:
+        return None, 0
+    lib = load()
+    p = make_params(params)
+    need = int(lib.bokt_gemm_workspace_bytes(kernel, ctypes.byref(p)))
+    if need < 0:
+        check(BOKT_ERR_CUDA_RC, "bokt_gemm_workspace_bytes")
+    key = device if isinstance(device, int) else torch.device(device).index
+    buf = _splitk_ws.get(key)
+    if buf is None or buf.numel() < need:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("split-K workspace must be allocated before graph capture: "
+                               "make one uncaptured call with these parameters first")
+        buf = torch.zeros(need, dtype=torch.uint8, device=torch.device("cuda", key))
+        _splitk_ws[key] = buf
+    return ctypes.c_void_p(buf.data_ptr()), buf.numel()
+
+
+def splitk_schedule(ntiles, split_k, nkb, launched):
+    """Segments of the split-K schedule, computed by the library's own host
+    copy of the device arithmetic: list of (worker, tile, kb0, kb1,
+    first_contributor, contributors)."""
+    lib = load()
+    n = lib.bokt_splitk_schedule(ntiles, split_k, nkb, launched, None, 0)
+    if n < 0:
+        raise RuntimeError(lib.bokt_last_error().decode())
+    buf = (ctypes.c_int32 * (6 * max(n, 1)))()
+    lib.bokt_splitk_schedule(ntiles, split_k, nkb, launched, buf, n)
+    return [tuple(buf[6 * i:6 * i + 6]) for i in range(n)]
 
 
 _attr_cache = {}

@@ -16,6 +16,12 @@ kernels:
   tcgen05 cta_group::2, 256-row tiles).  For the MoE grouped GEMM, 2 cuts each
   expert into 256-row pair tiles and a last block of at most 128 rows as a
   half-height pair tile (M = 128), so padding stays that of 128-row tiles.
+* ``SPLIT_K`` 1 gives every tile one worker for its whole K loop (the
+  reference's kernel, ``kernels/gemm.py:31-39``); S > 1 cuts each tile's K loop
+  into S slices and deals the (tile, slice) units to the persistent CTAs in
+  contiguous runs (split-K / stream-K), the worker holding a tile's first slice
+  adding the others' fp32 partials.  Single-CTA grouped tiles or dense tiles
+  only (grouped CTA pairs are pruned).
 * MoE grouped GEMM only: ``RASTER`` 1 walks the tiles expert by expert; 2 spreads
   the tiles of experts with at most two 128-row blocks (weights read once or
   twice: HBM-bound) evenly between the tiles of the others (tensor-bound).
@@ -32,7 +38,7 @@ from dataclasses import asdict, dataclass
 from itertools import product
 from math import isfinite, prod
 
-SPACE_VERSION = 2
+SPACE_VERSION = 3
 KERNELS = ("gemm", "rmsnorm", "moe_grouped_gemm")
 
 
@@ -106,6 +112,7 @@ def search_space(kernel: str, profile: str = "full") -> dict[str, list[int]]:
         if profile == "full":
             space["RASTER"] = [1, 2]
             space["CTA_GROUP"] = [1, 2]
+    space["SPLIT_K"] = [1, 2, 4, 8, 16] if profile == "full" else [1, 4]
     return space
 
 
@@ -113,7 +120,8 @@ def default_params(kernel: str) -> dict[str, int]:
     """A good starting point on B200 (used by bench.py and as a tuning seed)."""
     if kernel == "rmsnorm":
         return {"ROWS_PER_CTA": 1, "num_warps": 4, "num_stages": 1}
-    p = {"BLOCK_M": 128, "BLOCK_N": 256, "BLOCK_K": 64, "num_warps": 6, "num_stages": 4}
+    p = {"BLOCK_M": 128, "BLOCK_N": 256, "BLOCK_K": 64, "num_warps": 6, "num_stages": 4,
+         "SPLIT_K": 1}
     if kernel == "gemm":
         p.update(GROUP_M=8, CTA_GROUP=2, num_stages=6)
     else:

@@ -205,7 +205,7 @@ const void* tc_kernel(bool grouped, int dtype, int bn, bool scatter = false,
 }
 
 struct TcConfig {
-  int bn, stages, group_m, smem, cta_group, raster;
+  int bn, stages, group_m, smem, cta_group, raster, split_k;
 };
 
 int resolve_tc_config(const bokt_params* p, bool grouped, int experts, int smem_optin,
@@ -221,9 +221,15 @@ int resolve_tc_config(const bokt_params* p, bool grouped, int experts, int smem_
   if (bn != 64 && bn != 128 && bn != 256)
     return fail(BOKT_ERR_CONFIG, "block_n must be 64, 128 or 256 (got %d)", bn);
   if (warps != 6) return fail(BOKT_ERR_CONFIG, "num_warps must be 6 (TMA, MMA, 4 epilogue)");
-  if (p->split_k > 1) return fail(BOKT_ERR_UNSUPPORTED, "split_k > 1 is not implemented");
+  const int split_k = param_or(p->split_k, 1);
+  if (split_k < 1 || split_k > bokt::kSplitKMax)
+    return fail(BOKT_ERR_CONFIG, "split_k must be in [1, %d] (got %d)", bokt::kSplitKMax, split_k);
   const int cta_group = param_or(p->cta_group, 1);
   if (cta_group != 1 && cta_group != 2) return fail(BOKT_ERR_CONFIG, "cta_group must be 1 or 2");
+  if (split_k > 1 && cta_group == 2 && grouped)
+    return fail(BOKT_ERR_CONFIG,
+                "split_k > 1 applies to the dense GEMM (single CTAs or pairs) and the "
+                "single-CTA grouped GEMM, not to grouped CTA pairs");
   if (cta_group == 2 && bn == 64)
     return fail(BOKT_ERR_CONFIG, "cta_group 2 needs block_n 128 or 256");
   const int raster = param_or(p->raster, bokt::kRasterExpert);
@@ -248,6 +254,35 @@ int resolve_tc_config(const bokt_params* p, bool grouped, int experts, int smem_
   out->smem = smem;
   out->cta_group = cta_group;
   out->raster = raster;
+  out->split_k = split_k;
+  return BOKT_OK;
+}
+
+// Split-K workspace of the current device: one slot per SM (no launch of a
+// split-K kernel uses more CTAs), sized for the configuration's BN.
+int64_t splitk_bytes_for(const DeviceInfo& dev, int bn) {
+  return bokt::splitk_workspace_bytes(dev.sm_count, bn);
+}
+
+// Attach the workspace to `args` for a split-K launch; checks size and alignment.
+int attach_splitk(const TcConfig& cfg, const DeviceInfo& dev, int nkb, void* ws, int64_t ws_bytes,
+                  GemmTcArgs* args) {
+  int split = cfg.split_k < nkb ? cfg.split_k : nkb;
+  if (split < 1) split = 1;
+  args->split_k = split;
+  if (split == 1) return BOKT_OK;
+  const int64_t need = splitk_bytes_for(dev, cfg.bn);
+  if (!ws)
+    return fail(BOKT_ERR_INVALID,
+                "split_k > 1 needs a workspace of %lld bytes (zero-filled once when allocated); "
+                "pass it to the _ex entry point", (long long)need);
+  if (ws_bytes < need)
+    return fail(BOKT_ERR_INVALID, "split-K workspace too small: %lld bytes, need %lld",
+                (long long)ws_bytes, (long long)need);
+  if ((reinterpret_cast<uintptr_t>(ws) & 255u) != 0)
+    return fail(BOKT_ERR_INVALID, "split-K workspace must be 256-byte aligned");
+  args->splitk_ws = ws;
+  args->splitk_slots = dev.sm_count;
   return BOKT_OK;
 }
 
@@ -329,7 +364,8 @@ bool tc_eligible(const void* A, const void* B, const void* C, int N, int K) {
 // Dense GEMM entry body.  row_scale != nullptr scales C row m by row_scale[m]
 // in the epilogue (the fused RMSNorm -> GEMM; tcgen05 path only).
 int dense_gemm_impl(const void* A, const void* B, void* C, int M, int N, int K, int dtype,
-                    const bokt_params* params, void* stream, const float* row_scale) {
+                    const bokt_params* params, void* stream, const float* row_scale,
+                    void* workspace = nullptr, int64_t workspace_bytes = 0) {
   if (dtype != BOKT_FP16 && dtype != BOKT_BF16) return fail(BOKT_ERR_INVALID, "dtype %d", dtype);
   if (M < 0 || N < 0 || K < 0) return fail(BOKT_ERR_INVALID, "negative size");
   if (M == 0 || N == 0) return BOKT_OK;
@@ -368,16 +404,20 @@ int dense_gemm_impl(const void* A, const void* B, void* C, int M, int N, int K, 
   args.group_m = cfg.group_m;
   args.stages = cfg.stages;
   args.row_scale = row_scale;
+  rc = attach_splitk(cfg, dev, (K + bokt::kGemmBK - 1) / bokt::kGemmBK, workspace,
+                     workspace_bytes, &args);
+  if (rc) return rc;
+  const long long split = args.split_k;
   if (cfg.cta_group == 2) {
     args.idesc = bokt::make_idesc_f16(uint32_t(dtype), 256, uint32_t(cfg.bn));
-    const long long tiles2 = (long long)((M + 255) / 256) * ((N + cfg.bn - 1) / cfg.bn);
+    const long long units = (long long)((M + 255) / 256) * ((N + cfg.bn - 1) / cfg.bn) * split;
     const long long max_pairs = dev.sm_count / 2;
-    const int pairs = int(tiles2 < max_pairs ? tiles2 : max_pairs);
+    const int pairs = int(units < max_pairs ? units : max_pairs);
     return launch_tc2(dtype, cfg, ma, mb, args, pairs, s);
   }
   args.idesc = bokt::make_idesc_f16(uint32_t(dtype), 128, uint32_t(cfg.bn));
-  const long long tiles = (long long)((M + 127) / 128) * ((N + cfg.bn - 1) / cfg.bn);
-  const int grid = int(tiles < dev.sm_count ? tiles : dev.sm_count);
+  const long long units = (long long)((M + 127) / 128) * ((N + cfg.bn - 1) / cfg.bn) * split;
+  const int grid = int(units < dev.sm_count ? units : dev.sm_count);
   return launch_tc(false, dtype, cfg, ma, mb, args, grid, s);
 }
 
@@ -494,6 +534,25 @@ int bokt_gemm(const void* A, const void* B, void* C, int M, int N, int K, int dt
   return dense_gemm_impl(A, B, C, M, N, K, dtype, params, stream, nullptr);
 }
 
+int bokt_gemm_ex(const void* A, const void* B, void* C, int M, int N, int K, int dtype,
+                 const bokt_params* params, void* workspace, int64_t workspace_bytes,
+                 void* stream) {
+  g_err[0] = 0;
+  return dense_gemm_impl(A, B, C, M, N, K, dtype, params, stream, nullptr, workspace,
+                         workspace_bytes);
+}
+
+int64_t bokt_gemm_workspace_bytes(int kernel, const bokt_params* params) {
+  g_err[0] = 0;
+  if (kernel != BOKT_KERNEL_GEMM && kernel != BOKT_KERNEL_MOE_GROUPED_GEMM) return 0;
+  const bokt_params zero = {};
+  const bokt_params* p = params ? params : &zero;
+  if (param_or(p->split_k, 1) <= 1) return 0;
+  DeviceInfo dev;
+  if (device_info(&dev)) return -1;
+  return splitk_bytes_for(dev, param_or(p->block_n, 256));
+}
+
 int bokt_rmsnorm_fold_weight(const void* norm_weight, const void* B, void* B_folded, int K, int N,
                              int dtype, void* stream) {
   g_err[0] = 0;
@@ -584,7 +643,8 @@ struct ScatterArgs {
 
 int grouped_gemm_impl(const void* X, const void* W, const void* offsets, int offsets_is_i64,
                       void* Y, int T, int E, int N, int K, int dtype, int sm_count,
-                      const bokt_params* params, void* stream, const ScatterArgs* scatter) {
+                      const bokt_params* params, void* stream, const ScatterArgs* scatter,
+                      void* workspace = nullptr, int64_t workspace_bytes = 0) {
   if (dtype != BOKT_FP16 && dtype != BOKT_BF16) return fail(BOKT_ERR_INVALID, "dtype %d", dtype);
   if (T < 0 || E < 0 || N < 0 || K < 0) return fail(BOKT_ERR_INVALID, "negative size");
   if (E > bokt::kGemmMaxExperts)
@@ -656,10 +716,14 @@ int grouped_gemm_impl(const void* X, const void* W, const void* offsets, int off
     return launch_tc2(dtype, cfg, ma, mb, pa, int(pairs), s, /*grouped=*/true, scatter != nullptr,
                       &ma64);
   }
+  rc = attach_splitk(cfg, dev, (K + bokt::kGemmBK - 1) / bokt::kGemmBK, workspace,
+                     workspace_bytes, &args);
+  if (rc) return rc;
   // Upper bound on tiles without reading offsets: sum_e cdiv(c_e, 128) <= cdiv(T, 128) + E.
   const long long max_tiles = ((long long)(T + 127) / 128 + E) * nn;
   long long grid = (long long)sms * mult;
-  if (grid > max_tiles) grid = max_tiles;
+  if (args.split_k > 1 && grid > dev.sm_count) grid = dev.sm_count;  // one slot per CTA
+  if (grid > max_tiles * args.split_k) grid = max_tiles * args.split_k;
   if (grid < 1) grid = 1;
   return launch_tc(true, dtype, cfg, ma, mb, args, int(grid), s, scatter != nullptr);
 }
@@ -674,6 +738,15 @@ int bokt_moe_grouped_gemm(const void* X, const void* W, const void* offsets, int
   g_err[0] = 0;
   return grouped_gemm_impl(X, W, offsets, offsets_is_i64, Y, T, E, N, K, dtype, sm_count, params,
                            stream, nullptr);
+}
+
+int bokt_moe_grouped_gemm_ex(const void* X, const void* W, const void* offsets,
+                             int offsets_is_i64, void* Y, int T, int E, int N, int K, int dtype,
+                             int sm_count, const bokt_params* params, void* workspace,
+                             int64_t workspace_bytes, void* stream) {
+  g_err[0] = 0;
+  return grouped_gemm_impl(X, W, offsets, offsets_is_i64, Y, T, E, N, K, dtype, sm_count, params,
+                           stream, nullptr, workspace, workspace_bytes);
 }
 
 int bokt_moe_grouped_gemm_scatter(const void* X, const void* W, const void* offsets,
@@ -1102,6 +1175,36 @@ int bokt_kernel_attrs(int kernel, int dtype, int n, int k, const bokt_params* pa
   out->max_threads = a.maxThreadsPerBlock;
   out->path = path;
   return BOKT_OK;
+}
+
+int bokt_splitk_schedule(int ntiles, int split_k, int nkb, int launched, int32_t* out,
+                         int capacity) {
+  g_err[0] = 0;
+  if (ntiles < 0 || split_k < 1 || nkb < 1 || launched < 1 || capacity < 0 || (!out && capacity))
+    return -fail(BOKT_ERR_INVALID, "bad argument");
+  const int split = split_k < nkb ? split_k : nkb;
+  const int workers = bokt::splitk_workers(launched, ntiles, split);
+  int n = 0;
+  for (int w = 0; w < launched; ++w) {
+    bokt::SegmentCursor cur = bokt::segment_cursor(w, workers, ntiles, split);
+    bokt::Segment sg;
+    while (bokt::segment_next(cur, split, nkb, sg)) {
+      int first = 0, count = 0;
+      if (split > 1 && sg.kb0 == 0 && sg.kb1 < nkb)
+        count = bokt::splitk_contributors(w, workers, ntiles, split, sg.tile, &first);
+      if (n < capacity) {
+        int32_t* r = out + 6 * static_cast<int64_t>(n);
+        r[0] = w;
+        r[1] = sg.tile;
+        r[2] = sg.kb0;
+        r[3] = sg.kb1;
+        r[4] = first;
+        r[5] = count;
+      }
+      ++n;
+    }
+  }
+  return n;
 }
 
 int bokt_device_status(int* code, int* detail, int reset) {

@@ -18,6 +18,7 @@
 #pragma once
 
 #include "bokt_device.cuh"
+#include "splitk.cuh"
 
 namespace bokt {
 
@@ -54,6 +55,12 @@ struct GemmTcArgs {
   // inside an expert); kRasterBalanced spreads the tiles of low-reuse experts
   // (at most kLowReuseMBlocks row blocks) evenly between the others.
   int raster;
+  // Split-K (splitk.cuh): split_k k-slices per tile, dealt out in contiguous
+  // runs; the fp32 partials of non-owner segments go through splitk_ws, a
+  // workspace of splitk_slots CTA slots.  split_k == 1: whole tiles.
+  int split_k;
+  void* splitk_ws;
+  int splitk_slots;
 };
 
 constexpr int kRasterExpert = 1;
@@ -89,16 +96,24 @@ __host__ __device__ inline int gemm_tc_smem_bytes(int bn, int stages, bool group
 // is written back with every group of 8 lanes storing one full 128-byte row
 // segment: coalesced HBM writes, and full-line NVLink writes when a row
 // pointer is a peer GPU's memory.
+//
+// Split-K owners: `pcount` fp32 partial tiles (the first at `pfirst`, the next
+// `pstep` floats apart; splitk.cuh layout, slot row `prow`) are added to the
+// accumulator before scaling and rounding, in slot order.
 template <int BN, typename OutT, bool SCALED = false>
 __device__ __forceinline__ void epilogue_store_tile(uint32_t taddr, uint8_t* stage,
                                                     OutT* const* rowptr, int n0, int N,
-                                                    int lane, float scale = 1.f) {
+                                                    int lane, float scale = 1.f,
+                                                    const float* pfirst = nullptr,
+                                                    int64_t pstep = 0, int pcount = 0,
+                                                    int prow = 0) {
 #pragma unroll 1
   for (int c = 0; c < BN; c += 64) {
     uint32_t v0[32], v1[32];
     tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c), v0);
     tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c + 32), v1);
     tmem_ld_wait();
+    if (pcount > 0) splitk_add_partials(v0, v1, pfirst, pstep, pcount, prow, c);
     uint8_t* my_row = stage + lane * 128;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -384,15 +399,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if constexpr (GROUPED) {
     build_grouped_schedule(args, nn, sched);
   }
+  const int split = args.split_k > 1 ? args.split_k : 1;
+  SplitKView sk = {};
+  if (split > 1) {
+    sk = splitk_view(args.splitk_ws, args.splitk_slots, BN);
+    // Sequence number of this launch (+1): the value the partial flags carry.
+    if (threadIdx.x == 0) tmem_holder[2] = ld_acquire_gpu(sk.header) + 1u;
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  const uint32_t expected = tmem_holder[2];
   if constexpr (GROUPED) {
     ntiles = sched.totals[0];
   } else {
     ntiles = ((args.M + kGemmBM - 1) / kGemmBM) * nn;
   }
+  const int workers = splitk_workers(gridDim.x, ntiles, split);
+  const int worker = blockIdx.x;
 
   auto tile_at = [&](int t) -> TileCoord {
     if constexpr (GROUPED) {
@@ -408,9 +433,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-        const TileCoord tc = tile_at(t);
-        for (int kb = 0; kb < nkb; ++kb) {
+      SegmentCursor cur = segment_cursor(worker, workers, ntiles, split);
+      Segment sg;
+      while (ok && segment_next(cur, split, nkb, sg)) {
+        const TileCoord tc = tile_at(sg.tile);
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, 1)) {
             ok = false;
             break;
@@ -442,13 +469,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       int i = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++i) {
+      SegmentCursor cur = segment_cursor(worker, workers, ntiles, split);
+      Segment sg;
+      for (; ok && segment_next(cur, split, nkb, sg); ++i) {
         const int acc = i & 1;
         const uint32_t acc_phase = (static_cast<uint32_t>(i) >> 1) & 1u;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, 2)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < nkb; ++kb) {
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, 3)) {
             ok = false;
             break;
@@ -463,7 +492,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             // B: N-major; a K16 step is two 8-row groups (2 x 1024 bytes);
             // 64-column boxes sit 64 rows x 128 bytes apart.
             const uint64_t b_desc = smem_desc_sw128(b_addr + k * 2048, 64 * 128, 1024);
-            umma_f16_ss(d_tmem, a_desc, b_desc, args.idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_f16_ss(d_tmem, a_desc, b_desc, args.idesc,
+                        (kb != sg.kb0 || k != 0) ? 1u : 0u);
           }
           umma_commit(&empty[stage]);
           if (++stage == stages) {
@@ -482,9 +512,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     OutT* C = reinterpret_cast<OutT*>(args.C);
     uint8_t* stage = sEpi + (warp - 2) * kEpiStageBytes;
     OutT** rowptr = reinterpret_cast<OutT**>(sEpi + kEpiWarps * kEpiStageBytes) + (warp - 2) * 32;
+    const int64_t slot_floats = static_cast<int64_t>(kGemmBM) * BN;
     int i = 0;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
-      const TileCoord tc = tile_at(t);
+    SegmentCursor cur = segment_cursor(worker, workers, ntiles, split);
+    Segment sg;
+    for (; segment_next(cur, split, nkb, sg); ++i) {
+      const TileCoord tc = tile_at(sg.tile);
       const int acc = i & 1;
       const uint32_t acc_phase = (static_cast<uint32_t>(i) >> 1) & 1u;
       const bool ok = mbar_wait(&tfull[acc], acc_phase, abort_flag, 4);
@@ -492,6 +525,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      if (sg.kb0 > 0) {
+        // Split-K non-owner: this worker's first segment; publish the fp32
+        // partial rows of this warp into the CTA's slot.
+        epilogue_store_partial<BN>(taddr, sk.partials + slot_floats * worker, q * 32, 0, lane);
+        splitk_publish(sk.flags, worker, q, expected, lane);
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+        continue;
+      }
+      int first = 0, count = 0;
+      if (sg.kb1 < nkb) {
+        count = splitk_contributors(worker, workers, ntiles, split, sg.tile, &first);
+        count = splitk_acquire(sk.flags, first, 1, count, q, expected, lane, 21);
+      }
       bool row_ok = r < tc.rows_valid;
       OutT* crow = C + static_cast<size_t>(tc.c_row + (row_ok ? r : 0)) * N + tc.n0;
       if constexpr (SCATTER) {
@@ -511,7 +558,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       float scale = 1.f;
       if constexpr (ROWSCALE) scale = row_ok ? args.row_scale[tc.c_row + r] : 1.f;
       __syncwarp();
-      epilogue_store_tile<BN, OutT, ROWSCALE>(taddr, stage, rowptr, tc.n0, N, lane, scale);
+      epilogue_store_tile<BN, OutT, ROWSCALE>(taddr, stage, rowptr, tc.n0, N, lane, scale,
+                                              sk.partials + slot_floats * first, slot_floats,
+                                              count, r);
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
     }
@@ -521,6 +570,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // ---------------------------------------------------------------- teardown
   tc_fence_before();
   __syncthreads();
+  if (split > 1 && threadIdx.x == 0) splitk_finish(sk.header, expected);
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();

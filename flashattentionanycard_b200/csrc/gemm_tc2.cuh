@@ -113,11 +113,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // Every CTA builds the same schedule (cluster_sync publishes it).
     build_grouped_schedule(args, nn, sched, 2 * kGemmBM);
   }
+  // Split-K (dense pairs only): workers are CTA pairs; CTA r of pair p uses
+  // workspace slot 2 p + r for the 128 accumulator rows it holds.
+  const int split = args.split_k > 1 ? args.split_k : 1;
+  SplitKView sk = {};
+  if (split > 1) {
+    sk = splitk_view(args.splitk_ws, args.splitk_slots, BN);
+    if (threadIdx.x == 0) tmem_holder[2] = ld_acquire_gpu(sk.header) + 1u;
+  }
   tc_fence_before();
   cluster_sync();  // both CTAs' barriers initialised, TMEM allocated, schedule built
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  const uint32_t expected = tmem_holder[2];
   const int ntiles = GROUPED ? sched.totals[0] : nm * nn;
+  const int workers = splitk_workers(npairs, ntiles, split);
 
   // 256-row tiles: dense in the GROUP_M raster of kernels/gemm.py:20-26;
   // grouped inside each expert (rows_valid = rows of the expert in the tile).
@@ -146,9 +156,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int t = pair; t < ntiles && ok; t += npairs) {
-        const TileCoord tc = tile_at(t);
-        for (int kb = 0; kb < nkb; ++kb) {
+      SegmentCursor cur = segment_cursor(pair, workers, ntiles, split);
+      Segment sg;
+      while (ok && segment_next(cur, split, nkb, sg)) {
+        const TileCoord tc = tile_at(sg.tile);
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
           if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, abort_flag, 11)) {
             ok = false;
             break;
@@ -190,17 +202,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       int i = 0;
       bool ok = true;
-      for (int t = pair; t < ntiles && ok; t += npairs, ++i) {
+      SegmentCursor cur = segment_cursor(pair, workers, ntiles, split);
+      Segment sg;
+      for (; ok && segment_next(cur, split, nkb, sg); ++i) {
         uint32_t idesc = args.idesc;
         if constexpr (GROUPED) {
-          if (tile_at(t).rows_valid <= kGemmBM) idesc = args.idesc_half;
+          if (tile_at(sg.tile).rows_valid <= kGemmBM) idesc = args.idesc_half;
         }
         const int acc = i & 1;
         const uint32_t acc_phase = (static_cast<uint32_t>(i) >> 1) & 1u;
         if (!mbar_wait_cluster(&tempty[acc], acc_phase ^ 1u, abort_flag, 12)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < nkb; ++kb) {
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
           if (!mbar_wait_cluster(&full[stage], phase, abort_flag, 13)) {
             ok = false;
             break;
@@ -212,7 +226,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           for (int k = 0; k < kGemmBK / 16; ++k) {
             const uint64_t a_desc = smem_desc_sw128(a_addr + k * 32, 16, 1024);
             const uint64_t b_desc = smem_desc_sw128(b_addr + k * 2048, 64 * 128, 1024);
-            umma_f16_ss_pair(d_tmem, a_desc, b_desc, idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_f16_ss_pair(d_tmem, a_desc, b_desc, idesc, (kb != sg.kb0 || k != 0) ? 1u : 0u);
           }
           umma_commit_both(&empty[stage]);
           if (++stage == stages) {
@@ -231,9 +245,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     OutT* C = reinterpret_cast<OutT*>(args.C);
     uint8_t* stage = sEpi + (warp - 2) * kEpiStageBytes;
     OutT** rowptr = reinterpret_cast<OutT**>(sEpi + kEpiWarps * kEpiStageBytes) + (warp - 2) * 32;
+    const int64_t slot_floats = static_cast<int64_t>(kGemmBM) * BN;
+    const int my_slot = 2 * pair + static_cast<int>(rank);
     int i = 0;
-    for (int t = pair; t < ntiles; t += npairs, ++i) {
-      const TileCoord tc = tile_at(t);
+    SegmentCursor cur = segment_cursor(pair, workers, ntiles, split);
+    Segment sg;
+    for (; segment_next(cur, split, nkb, sg); ++i) {
+      const TileCoord tc = tile_at(sg.tile);
       const int acc = i & 1;
       const uint32_t acc_phase = (static_cast<uint32_t>(i) >> 1) & 1u;
       const bool ok = mbar_wait_cluster(&tfull[acc], acc_phase, abort_flag, 14);
@@ -241,6 +259,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      if (sg.kb0 > 0) {
+        // Split-K non-owner (this pair's first segment): publish this warp's
+        // fp32 partial rows into the CTA's slot.
+        epilogue_store_partial<BN>(taddr, sk.partials + slot_floats * my_slot, q * 32, 0, lane);
+        splitk_publish(sk.flags, my_slot, q, expected, lane);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(map_shared(smem_addr(&tempty[acc]), 0));
+        continue;
+      }
+      int first = 0, count = 0;
+      if (sg.kb1 < nkb) {
+        count = splitk_contributors(pair, workers, ntiles, split, sg.tile, &first);
+        count = splitk_acquire(sk.flags, 2 * first + static_cast<int>(rank), 2, count, q,
+                               expected, lane, 22);
+      }
+      const float* pfirst = sk.partials + slot_floats * (2 * first + static_cast<int>(rank));
       // Full tile: this CTA's accumulator rows are tile rows [128 rank, +128),
       // warp quadrant q holds rows 32 q .. 32 q + 31, all BN columns.
       // Half tile (grouped): this CTA's rows are [64 rank, +64); quadrant q holds
@@ -272,7 +307,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (half) {
         epilogue_store_tile<BN / 2, OutT, ROWSCALE>(taddr, stage, rowptr, col0, N, lane, scale);
       } else {
-        epilogue_store_tile<BN, OutT, ROWSCALE>(taddr, stage, rowptr, col0, N, lane, scale);
+        epilogue_store_tile<BN, OutT, ROWSCALE>(taddr, stage, rowptr, col0, N, lane, scale,
+                                                pfirst, 2 * slot_floats, count, r);
       }
       tc_fence_before();
       __syncwarp();
@@ -284,6 +320,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // ---------------------------------------------------------------- teardown
   tc_fence_before();
   __syncthreads();
+  if (split > 1 && threadIdx.x == 0) splitk_finish(sk.header, expected);
   cluster_sync();  // no CTA leaves while its peer may still signal its barriers
   if (warp == 1) {
     __syncwarp();

@@ -4,7 +4,11 @@ Drop-in for the reference's ``bo_kernel_tuner/kernels/gemm.py:43-48``: same
 ``launch(a, b, out, params)`` signature and meaning (C[M,N] = A[M,K] @ B[K,N],
 row-major contiguous, result rounded to ``out``'s dtype, every element of
 ``out`` written).  The tile order follows the reference's GROUP_M raster
-(``gemm.py:20-26``) inside a persistent warp-specialised kernel.
+(``gemm.py:20-26``) inside a persistent warp-specialised kernel.  With
+``SPLIT_K`` > 1 the K loop of every tile is split across workers (split-K /
+stream-K); the fp32 partials go through a per-device workspace allocated on
+the first such call (``_native.splitk_workspace``), so that first call must
+come before any graph capture.
 """
 
 import ctypes
@@ -26,9 +30,10 @@ def launch(a, b, out, params):
     lib = _native.load()
     dtype = _native.dtype_code(a.dtype)
     p = _native.make_params(params)
+    ws, ws_bytes = _native.splitk_workspace(_native.KERNEL_GEMM, params, a.device)
     _native.check(
-        lib.bokt_gemm(a.data_ptr(), b.data_ptr(), out.data_ptr(), m, n, k, dtype,
-                      ctypes.byref(p), _native.current_stream(a.device)),
+        lib.bokt_gemm_ex(a.data_ptr(), b.data_ptr(), out.data_ptr(), m, n, k, dtype,
+                         ctypes.byref(p), ws, ws_bytes, _native.current_stream(a.device)),
         "bokt_gemm",
     )
     return _native.kernel_attrs(_native.KERNEL_GEMM, dtype, n, k, params, a.device.index)

@@ -7,7 +7,9 @@ expert e, ``out[off[e]:off[e+1]] = x[off[e]:off[e+1]] @ weights[e]`` with
 reference's worker builds them, or int32 as the routing kernels produce them)
 stays on the device and is read by the kernel.  Empty experts cost nothing,
 every output tile has exactly one writer, and the persistent grid is
-``sm_count * CTA_MULTIPLIER`` CTAs as in the reference.
+``sm_count * CTA_MULTIPLIER`` CTAs as in the reference.  ``SPLIT_K`` > 1
+(single-CTA tiles) splits every tile's K loop across CTAs, with the fp32
+partials in a per-device workspace allocated on the first such call.
 
 Routing, sorting and scatter stay outside this operator, as in the reference
 (``moe_grouped_gemm.py:3``); the device routing front end lives in
@@ -42,11 +44,12 @@ def launch(x, weights, offsets, out, params, sm_count):
     lib = _native.load()
     dtype = _native.dtype_code(x.dtype)
     p = _native.make_params(params)
+    ws, ws_bytes = _native.splitk_workspace(_native.KERNEL_MOE_GROUPED_GEMM, params, x.device)
     _native.check(
-        lib.bokt_moe_grouped_gemm(
+        lib.bokt_moe_grouped_gemm_ex(
             x.data_ptr(), weights.data_ptr(), offsets.data_ptr(),
             1 if offsets.dtype == torch.int64 else 0, out.data_ptr(), t, e, n, k, dtype,
-            int(sm_count), ctypes.byref(p), _native.current_stream(x.device),
+            int(sm_count), ctypes.byref(p), ws, ws_bytes, _native.current_stream(x.device),
         ),
         "bokt_moe_grouped_gemm",
     )

@@ -181,6 +181,9 @@ def prune_reason(hardware, kernel, params, columns=0, heuristic_smem=False):
     pair = params.get("CTA_GROUP", 1) == 2
     if pair and params["BLOCK_N"] == 64:
         return "illegal_tile_shape"
+    split = params.get("SPLIT_K", 1)
+    if split < 1 or split > 32 or (split > 1 and pair and kernel == "moe_grouped_gemm"):
+        return "illegal_split_k"
     experts = 64 if kernel == "moe_grouped_gemm" else 0
     smem = (gemm_pair_shared_bytes(params["BLOCK_N"], params["num_stages"], experts) if pair
             else gemm_shared_bytes(params["BLOCK_N"], params["num_stages"], experts))

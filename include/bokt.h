@@ -86,7 +86,8 @@ typedef struct bokt_params {
   int32_t cta_multiplier;
   int32_t num_warps;
   int32_t rows_per_cta;
-  int32_t split_k;   /* reserved: must be 0 or 1 */
+  int32_t split_k;   /* 0/1: one worker runs a tile's whole K loop; 2..32: split-K /
+                        stream-K (see bokt_gemm_ex); needs a workspace */
   int32_t cta_group; /* 0/1: one CTA per tile; 2: CTA pairs (dense GEMM) */
   int32_t raster;    /* grouped GEMM tile order: 0/1 expert order, 2 balanced
                         (low-reuse experts spread between the others) */
@@ -118,6 +119,46 @@ const char* bokt_last_error(void);
  */
 int bokt_gemm(const void* A, const void* B, void* C, int M, int N, int K, int dtype,
               const bokt_params* params, void* stream);
+
+/*
+ * bokt_gemm with a split-K workspace.  params->split_k = S > 1 cuts every
+ * tile's K loop into S slices of nearly equal k-block counts (S is clamped to
+ * the number of 64-wide k-blocks) and deals the (tile, slice) units out to the
+ * persistent CTAs (or CTA pairs) in contiguous runs, so every worker gets the
+ * same number of k-block iterations even when the tile count is not a multiple
+ * of the SM count; S = number of k-blocks is stream-K.  The worker that holds a
+ * tile's first slice adds the other workers' fp32 partial tiles (read from the
+ * workspace, in worker order: deterministic) and writes C.  The K loop being
+ * split is the one of kernels/gemm.py:31-39 in the reference; the parameter is
+ * the split-K entry of the redefined search space (configs/search_spaces.py:48-75).
+ *
+ * workspace: device memory of bokt_gemm_workspace_bytes(BOKT_KERNEL_GEMM,
+ * params) bytes (about 19 MB at block_n 256 on a 148-SM B200), 256-byte
+ * aligned and zero-filled ONCE when it is allocated; the library keeps a
+ * launch sequence number in it, so it is not cleared between calls.  Calls
+ * that share a workspace must not overlap on the GPU (use one per stream).
+ * With split_k <= 1 the workspace may be NULL and the call equals bokt_gemm.
+ */
+int bokt_gemm_ex(const void* A, const void* B, void* C, int M, int N, int K, int dtype,
+                 const bokt_params* params, void* workspace, int64_t workspace_bytes,
+                 void* stream);
+
+/* Workspace bytes for a split-K launch of `kernel` (BOKT_KERNEL_GEMM or
+ * BOKT_KERNEL_MOE_GROUPED_GEMM) with `params` on the current device; 0 when
+ * params->split_k <= 1, -1 on error. */
+int64_t bokt_gemm_workspace_bytes(int kernel, const bokt_params* params);
+
+/*
+ * Inspection of the split-K schedule (host only, no GPU work): for `ntiles`
+ * output tiles of `nkb` k-blocks, split_k slices per tile and `launched`
+ * workers, writes one record of 6 int32 per segment into out[6 * i ..]:
+ * {worker, tile, first k-block, one past the last k-block, first contributor
+ * worker, contributor count} (contributors only for a tile's owner segment).
+ * Returns the number of segments (records beyond `capacity` are not written),
+ * or a negative status.  Exposes the exact arithmetic the kernels run.
+ */
+int bokt_splitk_schedule(int ntiles, int split_k, int nkb, int launched, int32_t* out,
+                         int capacity);
 
 /*
  * Y[M,N] = X * rsqrt(mean(X^2, -1) + eps) * W, fp32 arithmetic, one pass over X.
@@ -160,6 +201,13 @@ int bokt_rmsnorm_gemm(const void* X, const void* B_folded, void* C, float* row_s
 int bokt_moe_grouped_gemm(const void* X, const void* W, const void* offsets, int offsets_is_i64,
                           void* Y, int T, int E, int N, int K, int dtype, int sm_count,
                           const bokt_params* params, void* stream);
+
+/* bokt_moe_grouped_gemm with a split-K workspace (bokt_gemm_ex semantics;
+ * split_k > 1 with single-CTA tiles only, cta_group 1). */
+int bokt_moe_grouped_gemm_ex(const void* X, const void* W, const void* offsets,
+                             int offsets_is_i64, void* Y, int T, int E, int N, int K, int dtype,
+                             int sm_count, const bokt_params* params, void* workspace,
+                             int64_t workspace_bytes, void* stream);
 
 /*
  * Routing front end for A = tokens * topk assignments given as expert ids
