@@ -16,7 +16,15 @@ Samplers: with Optuna installed, the reference's grid / random / multivariate
 TPE over an sqlite study.  Without it (this image has none), grid and random
 run on a built-in driver with the same accounting and outputs; TPE and warm
 starts require Optuna.
+
+``warm_start`` turns a finished search into a TPE warm-start queue (the
+reference's rank-based transfer, ``tuner/transfer.py:11-54``), and ``main`` is a
+small command line over this engine.  The reference's own ``run_benchmark``
+CLI, engine and worker drive these kernels unchanged through
+``flashattentionanycard_b200.dropin`` when the reference is installed.
 """
+
+import argparse
 
 import csv
 import hashlib
@@ -399,3 +407,119 @@ def _run_optuna(space, method, seed, startup_trials, warm_params, attempts, time
     finally:
         data = export(snapshot(), output, metadata, status, time.perf_counter() - start)
     return data
+
+
+# ----------------------------------------------------------------------------- warm start
+def _usable(trial):
+    value = trial.get("value")
+    return (trial.get("state") == "COMPLETE" and isinstance(value, (int, float))
+            and math.isfinite(value) and value > 0)
+
+
+def warm_start(result_path, workload, space, top_k, hardware, prune):
+    """TPE warm-start queue from a finished search: the ``top_k`` fastest
+    distinct configurations of the source that are legal here.
+
+    Only the source's ranking transfers, never its latencies: the queued
+    configurations are measured again on this device.  The source must be a
+    complete schema-1 result for the same workload signature, search space and
+    code fingerprint (kernels, search space and measurement code unchanged).
+    ``prune(params)`` returns a reason (truthy) for configurations illegal on
+    the target.  Returns (queue, provenance)."""
+    if top_k < 1:
+        raise ValueError("top_k must be at least 1")
+    raw = Path(result_path).read_bytes()
+    source = json.loads(raw)
+    if source.get("schema_version") != 1 or source.get("status") != "complete":
+        raise ValueError("Warm start needs a complete schema-1 search result")
+    meta = source.get("metadata", {})
+    if meta.get("workload") != workload.signature() or meta.get("search_space") != space:
+        raise ValueError("Warm start source workload or search space mismatch")
+    if meta.get("code_fingerprint") != code_fingerprint():
+        raise ValueError("Warm start source was measured with different kernel code")
+    queue = []
+    for trial in sorted(filter(_usable, source.get("trials", [])), key=lambda t: t["value"]):
+        params = trial["params"]
+        if params in queue or not validate_params(params, space) or prune(params):
+            continue
+        queue.append(params)
+        if len(queue) == top_k:
+            break
+    if not queue:
+        raise ValueError("No legal source configurations available")
+    provenance = {
+        "source_sha256": hashlib.sha256(raw).hexdigest(),
+        "source_hardware": meta.get("hardware"),
+        "target_hardware": hardware.to_dict(),
+        "requested_top_k": top_k,
+        "enqueued": len(queue),
+        "strategy": "ranked_parameters_remeasured_on_target",
+    }
+    return queue, provenance
+
+
+# ----------------------------------------------------------------------------- command line
+def main(argv=None):
+    """``python -m flashattentionanycard_b200.tuner.engine --kernel gemm --m 2048 ...``:
+    one search over the kernel's launch space, trials in fresh worker processes,
+    result.json / trials.csv in ``--output``."""
+    from flashattentionanycard_b200.configs.search_spaces import Workload, search_space
+    from flashattentionanycard_b200.tuner.hardware import Hardware
+
+    ap = argparse.ArgumentParser(description="Search the sm_100a kernels' launch parameters.")
+    ap.add_argument("--kernel", choices=("gemm", "rmsnorm", "moe_grouped_gemm"), default="gemm")
+    ap.add_argument("--dtype", choices=("fp16", "bf16"), default="bf16")
+    ap.add_argument("--m", type=int, default=1024)
+    ap.add_argument("--n", type=int, default=1024)
+    ap.add_argument("--k", type=int, default=1024)
+    ap.add_argument("--expert-tokens", default="64,128,256,512")
+    ap.add_argument("--epsilon", type=float, default=1e-6)
+    ap.add_argument("--data-seed", type=int, default=17)
+    ap.add_argument("--method", choices=("grid", "random", "tpe"), default="grid")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--trials", type=int, default=50)
+    ap.add_argument("--profile", choices=("full", "smoke"), default="full")
+    ap.add_argument("--output", type=Path, required=True)
+    ap.add_argument("--device", type=int, default=0)
+    ap.add_argument("--time-budget", type=float, default=None)
+    ap.add_argument("--trial-timeout", type=float, default=180)
+    ap.add_argument("--warm-start", type=Path, default=None, help="result.json of a finished search")
+    ap.add_argument("--top-k", type=int, default=5)
+    ap.add_argument("--measurement", default="20,30,32,2",
+                    help="warmup,repeats,batch,validation_seeds")
+    ap.add_argument("--dry-run", action="store_true", help="print the plan, touch no GPU")
+    args = ap.parse_args(argv)
+    try:
+        workload = Workload(args.kernel, args.m, args.n, args.k, args.dtype,
+                            tuple(int(x) for x in args.expert_tokens.split(",")), args.epsilon,
+                            args.data_seed)
+        space = search_space(args.kernel, args.profile)
+        measurement = Measurement(*(int(x) for x in args.measurement.split(",")))
+        if args.warm_start is not None and args.method != "tpe":
+            raise ValueError("--warm-start seeds a TPE search (--method tpe)")
+    except ValueError as exc:
+        print(f"error: {exc}", file=sys.stderr)
+        return 2
+    print(json.dumps({"workload": workload.signature(), "grid_size": grid_size(space),
+                      "method": args.method, "attempt_budget": min(args.trials, grid_size(space))}))
+    if args.dry_run:
+        return 0
+    hardware = Hardware.detect(args.device)
+    queue, provenance = (), None
+    if args.warm_start is not None:
+        queue, provenance = warm_start(
+            args.warm_start, workload, space, args.top_k, hardware,
+            lambda p: prune_reason(hardware, args.kernel, p, args.n))
+    result = run_search(workload, hardware, space, args.method, args.seed, args.trials,
+                        args.output, measurement, args.time_budget, args.trial_timeout,
+                        warm_params=queue, transfer=provenance)
+    best = result["best"]
+    print(json.dumps({"status": result["status"], "attempts": result["attempts"],
+                      "successful": result["successful_evaluations"],
+                      "best_ms": best["value"] if best else None,
+                      "best_params": best["params"] if best else None}))
+    return 0 if result["status"] == "complete" else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,6 +1,8 @@
 """Search engine, warm-start transfer and CLI (no GPU): mirrors the reference's
 tests/test_engine.py, with the evaluator injected and subprocess.run faked."""
 
+from flashattentionanycard_b200.tuner.engine import warm_start
+
 import json
 import subprocess
 import time
@@ -11,7 +13,6 @@ from flashattentionanycard_b200.configs.search_spaces import Workload, search_sp
 from flashattentionanycard_b200.tuner import engine
 from flashattentionanycard_b200.tuner.engine import EvaluationFailure, run_search
 from flashattentionanycard_b200.tuner.hardware import Hardware
-from flashattentionanycard_b200.tuner.transfer import load_warm_start
 from flashattentionanycard_b200.tuner.worker import Measurement
 
 SPACE = {"ROWS_PER_CTA": [1, 2], "num_warps": [4, 8]}
@@ -110,19 +111,20 @@ def test_tpe_needs_optuna_or_runs(tmp_path, hardware):
 def test_transfer_compatibility_and_pruning(tmp_path, hardware):
     search(tmp_path / "source", hardware, "grid")
     path = tmp_path / "source/result.json"
-    queue, provenance = load_warm_start(path, Workload("rmsnorm"), SPACE, 2, hardware,
-                                        lambda p: None)
+    queue, provenance = warm_start(path, Workload("rmsnorm"), SPACE, 2, hardware, lambda p: None)
     assert queue[0] == {"ROWS_PER_CTA": 1, "num_warps": 4} and len(queue) == 2
     assert provenance["strategy"] == "ranked_parameters_remeasured_on_target"
     with pytest.raises(ValueError, match="mismatch"):
-        load_warm_start(path, Workload("rmsnorm", n=7), SPACE, 2, hardware, lambda p: None)
+        warm_start(path, Workload("rmsnorm", n=7), SPACE, 2, hardware, lambda p: None)
     with pytest.raises(ValueError, match="No legal"):
-        load_warm_start(path, Workload("rmsnorm"), SPACE, 2, hardware, lambda p: "illegal")
+        warm_start(path, Workload("rmsnorm"), SPACE, 2, hardware, lambda p: "illegal")
+    with pytest.raises(ValueError, match="top_k"):
+        warm_start(path, Workload("rmsnorm"), SPACE, 0, hardware, lambda p: None)
     data = json.loads(path.read_text())
     data["metadata"]["code_fingerprint"] = "stale"
     path.write_text(json.dumps(data))
-    with pytest.raises(ValueError, match="code differ"):
-        load_warm_start(path, Workload("rmsnorm"), SPACE, 2, hardware, lambda p: None)
+    with pytest.raises(ValueError, match="different kernel code"):
+        warm_start(path, Workload("rmsnorm"), SPACE, 2, hardware, lambda p: None)
 
 
 def test_fingerprint_covers_cuda_sources(tmp_path, monkeypatch):
@@ -171,18 +173,15 @@ def test_wall_budget_stops_after_attempt(tmp_path, hardware):
     assert result["attempts"] < 20
 
 
-def test_cli_dry_run_and_invalid_options(tmp_path):
-    from typer.testing import CliRunner
-
-    from flashattentionanycard_b200.run_benchmark import app
-
-    runner = CliRunner()
-    result = runner.invoke(app, ["--dry-run", "--kernel", "moe_grouped_gemm", "--output",
-                                 str(tmp_path / "unused")])
-    assert result.exit_code == 0, result.output
-    assert not (tmp_path / "unused").exists()
-    result = runner.invoke(app, ["--dry-run", "--seeds", "0,0"])
-    assert result.exit_code == 2
+def test_cli_dry_run_and_invalid_options(tmp_path, capsys):
+    rc = engine.main(["--dry-run", "--kernel", "moe_grouped_gemm", "--output",
+                      str(tmp_path / "unused")])
+    assert rc == 0 and not (tmp_path / "unused").exists()
+    plan = json.loads(capsys.readouterr().out.strip().splitlines()[0])
+    assert plan["workload"]["kernel"] == "moe_grouped_gemm" and plan["grid_size"] > 0
+    assert engine.main(["--dry-run", "--expert-tokens", "0,0", "--kernel", "moe_grouped_gemm",
+                        "--output", str(tmp_path / "x")]) == 2
+    assert engine.main(["--dry-run", "--warm-start", "r.json", "--output", str(tmp_path)]) == 2
 
 
 def test_hardware_detect_requires_sm100_double():

@@ -1,5 +1,6 @@
 """The tuner plumbing end to end on the GPU: fresh worker process per trial
-(subprocess isolation), grid search over launch parameters, and the CLI."""
+(subprocess isolation), grid search over launch parameters, and the engine's
+command line."""
 
 import json
 
@@ -36,16 +37,12 @@ def test_grid_search_in_worker_processes(tmp_path, cuda_device):
 
 
 def test_cli_tune_run(tmp_path, cuda_device):
-    from typer.testing import CliRunner
-
-    from flashattentionanycard_b200.run_benchmark import app
-
     out = tmp_path / "study"
-    run = CliRunner().invoke(app, [
-        "--kernel", "moe_grouped_gemm", "--mode", "tune", "--method", "grid", "--dtype", "bf16",
-        "--n", "256", "--k", "128", "--expert-tokens", "0,1,33,0,9", "--seeds", "0",
-        "--trials", "2", "--profile", "smoke", "--warmup", "2", "--repeats", "3", "--batch", "2",
-        "--validation-seeds", "1", "--output", str(out), "--device", str(cuda_device.index)])
-    assert run.exit_code == 0, run.output
-    data = json.loads((out / "grid-seed-0" / "result.json").read_text())
+    rc = engine.main([
+        "--kernel", "moe_grouped_gemm", "--method", "grid", "--dtype", "bf16",
+        "--n", "256", "--k", "128", "--expert-tokens", "0,1,33,0,9", "--trials", "2",
+        "--profile", "smoke", "--measurement", "2,3,2,1", "--output", str(out),
+        "--device", str(cuda_device.index)])
+    assert rc == 0
+    data = json.loads((out / "result.json").read_text())
     assert data["status"] == "complete" and data["attempts"] == 2
