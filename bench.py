@@ -347,8 +347,9 @@ def moe_large_config(world):
            "params": params_for("moe_grouped_gemm")}
     if world > 1:
         _, p = moe_large_placement(c, world)
-        step = ("all-gather ids + route + NVLink peer-store dispatch + grouped GEMM with "
-                "peer-store combine epilogue, one-word all-reduce barriers, eager"
+        step = ("ids put to every rank + device barrier + route + NVLink peer-store dispatch "
+                "+ device barrier + grouped GEMM with peer-store combine epilogue + device "
+                "barrier; no host collective, steps captured in CUDA graphs"
                 if EP_COMM == "peer" else
                 "all-gather ids + route + dispatch all-to-all + grouped GEMM + "
                 "combine all-to-all (NCCL), eager")
@@ -777,10 +778,11 @@ class MoeLarge:
             self.ep = ep.PeerExpertParallelMoE(local, self.placement, self.plan, rank, world,
                                                cfg["topk"], tpr, group=dist.group.WORLD,
                                                params=self.params, sm_count=self.sm)
-            # route x3, plan, rowmap, dispatch, grouped GEMM with the peer-scatter epilogue
+            # put, 3 barriers, route x3, plan, rowmap, dispatch, grouped GEMM with the
+            # peer-scatter epilogue
             label, gemm_launches = grouped_kernel_label(self.params)
             self.kernel = label.replace(",grouped", ",grouped,scatter")
-            self.launches_per_step = 6 + gemm_launches
+            self.launches_per_step = 10 + gemm_launches
         else:
             self.ep = ep.ExpertParallelMoE(local, self.placement, self.plan, rank, world,
                                            cfg["topk"], tpr, group=dist.group.WORLD,
@@ -788,8 +790,9 @@ class MoeLarge:
             # routing/keys/sorts/checks + 4 gathers + grouped GEMM
             self.launches_per_step = 20 + grouped_kernel_label(self.params)[1]
         torch.cuda.empty_cache()
-        # Collectives between kernels: timed eagerly.
-        self.graphable = False
+        # Peer path: device barriers only, so whole steps are captured in CUDA
+        # graphs.  NCCL path: host collectives between kernels, timed eagerly.
+        self.graphable = self.comm == "peer"
         rows = int(self.placement.rank_rows[rank])
         self.kernel_flops = 2.0 * rows * cfg["k"] * cfg["n"]
         self.expected_counts = np.bincount(flat, minlength=cfg["experts"]).astype(np.int32)

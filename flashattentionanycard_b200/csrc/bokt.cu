@@ -12,6 +12,7 @@
 
 #include "../../include/bokt.h"
 #include "bokt_device.cuh"
+#include "ep_sync.cuh"
 #include "gemm_simt.cuh"
 #include "gemm_tc.cuh"
 #include "gemm_tc2.cuh"
@@ -805,6 +806,41 @@ int bokt_ep_dispatch(const void* x_local, int cols, int elem_bytes, const int32_
                          v_rank, v_plo, v_lbase, reinterpret_cast<uint4* const*>(xpk_ptrs),
                          capacity, a_local, topk, me, E);
   if (e != cudaSuccess) return cuda_fail(e, "ep_dispatch launch");
+  return BOKT_OK;
+}
+
+int bokt_ep_put(const void* src, int64_t bytes, void* const* dst_ptrs, int64_t dst_offset_bytes,
+                int world, void* stream) {
+  g_err[0] = 0;
+  if (bytes < 0 || dst_offset_bytes < 0 || world <= 0 || world > bokt::kEpMaxWorld)
+    return fail(BOKT_ERR_INVALID, "bad size");
+  if (bytes == 0) return BOKT_OK;
+  if (!src || !dst_ptrs) return fail(BOKT_ERR_INVALID, "null pointer");
+  if (bytes % 16 != 0 || dst_offset_bytes % 16 != 0 || !aligned16(src))
+    return fail(BOKT_ERR_UNSUPPORTED, "put needs 16-byte aligned source, size and offset");
+  const long long vecs = bytes / 16;
+  long long grid = (vecs + 255) / 256;
+  if (grid > 148 * 4) grid = 148 * 4;
+  cudaError_t e = launch(bokt::ep_put_kernel, dim3(unsigned(grid)), dim3(256), 0,
+                         static_cast<cudaStream_t>(stream), static_cast<const uint4*>(src),
+                         (long long)vecs, reinterpret_cast<uint4* const*>(dst_ptrs),
+                         (long long)(dst_offset_bytes / 16), world);
+  if (e != cudaSuccess) return cuda_fail(e, "ep_put launch");
+  return BOKT_OK;
+}
+
+int bokt_ep_barrier(int32_t* const* flag_ptrs, int32_t* epoch, int world, int me,
+                    int64_t timeout_ns, void* stream) {
+  g_err[0] = 0;
+  if (world <= 0 || world > bokt::kEpMaxWorld || me < 0 || me >= world)
+    return fail(BOKT_ERR_INVALID, "bad world/rank");
+  if (timeout_ns <= 0 || timeout_ns > 60000000000ll)
+    return fail(BOKT_ERR_INVALID, "timeout must be in (0, 60 s]");
+  if (!flag_ptrs || !epoch) return fail(BOKT_ERR_INVALID, "null pointer");
+  cudaError_t e = launch(bokt::ep_barrier_kernel, dim3(1), dim3(32), 0,
+                         static_cast<cudaStream_t>(stream), flag_ptrs, epoch, world, me,
+                         (long long)timeout_ns);
+  if (e != cudaSuccess) return cuda_fail(e, "ep_barrier launch");
   return BOKT_OK;
 }
 

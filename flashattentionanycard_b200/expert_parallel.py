@@ -323,37 +323,73 @@ def _ptr_array(ptrs, device):
     return torch.tensor([int(p) for p in ptrs], dtype=torch.int64, device=device)
 
 
+STATUS_MEANING = {
+    1: "a bounded wait timed out (detail: where; 4000 + r = expert-parallel barrier, rank r)",
+    2: "an expert id outside [0, E)",
+    3: "routing differs from the planned split sizes",
+    4: "a rank's packed buffer is too small for this step's routing",
+}
+
+
+def check_device_status(what):
+    """Raise RuntimeError if a kernel recorded a failure (synchronises the device)."""
+    code, detail = _native.device_status(reset=True)
+    if code:
+        raise RuntimeError(f"{what}: device status {code} ({STATUS_MEANING.get(code, '?')}), "
+                           f"detail {detail}")
+
+
 class PeerExpertParallelMoE:
     """One rank of the expert-parallel grouped GEMM with dispatch and combine
     over NVLink peer memory instead of NCCL all-to-all.
 
-    Each rank exports (CUDA IPC) its packed-input buffer and its output buffer
-    and maps the other ranks'.  A step:
+    Each rank exports (CUDA IPC) its packed-input, output, routing-id and
+    barrier-flag buffers and maps the other ranks'.  A step (``sync="device"``):
 
-      1. all-gather the expert ids (NCCL; also orders this step after every
-         rank's previous step);
+      1. bokt_ep_put: this rank's expert ids are stored into every rank's copy
+         of the global id table, then bokt_ep_barrier;
       2. global routing (bokt_moe_route) and the per-step layout (bokt_ep_plan):
          where each virtual expert's rows live on its rank;
       3. bokt_ep_rowmap: the owner row of every row this rank will compute;
       4. bokt_ep_dispatch: each token row is stored straight into the serving
-         rank's packed buffer (NVLink stores), then a one-word all-reduce
-         barrier;
+         rank's packed buffer (NVLink stores), then bokt_ep_barrier;
       5. bokt_moe_grouped_gemm_scatter: the tcgen05 grouped GEMM whose epilogue
          stores every result row into its token owner's output buffer (NVLink
-         stores, overlapped with the remaining tiles), then the barrier.
+         stores, overlapped with the remaining tiles), then bokt_ep_barrier.
 
+    Every phase is a kernel of this library and the barriers are device-side
+    (epochs in device memory, bounded waits), so the step has no host
+    collective, no host synchronisation and can be captured in a CUDA graph.
     No row gathers and no all-to-all: every row crosses NVLink once each way,
-    written by the kernel that produced it."""
+    written by the kernel that produced it.  ``sync="nccl"`` keeps the NCCL
+    all-gather and one-word all-reduce barriers instead.
+
+    Capacity: by default (``capacity="worst"``) each rank's packed buffer holds
+    every assignment of the step, so any routing fits whatever plan the
+    placement came from.  ``capacity="plan"`` sizes it from ``plan`` (less
+    memory); a step whose routing puts more rows on a rank then records
+    status 4 and drops those rows, which ``forward(..., check=True)`` turns
+    into an exception."""
 
     def __init__(self, local_weights, placement, plan, rank, world, topk, tokens_per_rank,
-                 group=None, params=None, sm_count=None, exchange=True):
+                 group=None, params=None, sm_count=None, exchange=True, sync=None,
+                 capacity="worst", barrier_timeout_s=5.0):
         """``exchange=False`` skips the IPC pointer exchange: the caller sets the
-        per-rank pointers with ``set_peer_pointers`` (ranks sharing one process)."""
+        per-rank pointers with ``set_peer_pointers`` (ranks sharing one process,
+        which drive the phases themselves: ``sync`` defaults to "none")."""
         import torch
 
         from flashattentionanycard_b200.kernels.moe_routing import MoeRouter
 
         lib = _native.load()
+        if sync is None:
+            sync = "device" if exchange else "none"
+        if sync not in ("device", "nccl", "none"):
+            raise ValueError("sync must be 'device', 'nccl' or 'none'")
+        if capacity not in ("worst", "plan"):
+            raise ValueError("capacity must be 'worst' or 'plan'")
+        self.sync = sync
+        self.barrier_timeout_ns = int(barrier_timeout_s * 1e9)
         self.rank, self.world, self.topk = rank, world, topk
         self.tokens_per_rank = tokens_per_rank
         self.group = group
@@ -376,7 +412,10 @@ class PeerExpertParallelMoE:
         self.replicas = torch.tensor(placement.replicas, **i32)
         self.vbase = torch.tensor(placement.vbase, **i32)
         self.v_rank = torch.tensor(placement.v_rank, **i32)
-        caps = [int(plan.local_rows[r].sum()) for r in range(world)]
+        if capacity == "worst":
+            caps = [self.a_global] * world
+        else:
+            caps = [int(plan.local_rows[r].sum()) for r in range(world)]
         self.capacity_rows = caps
         self.capacity = torch.tensor(caps, **i32)
         self.ids_global = torch.zeros(self.a_global, **i32)
@@ -392,23 +431,36 @@ class PeerExpertParallelMoE:
         self.x_packed = torch.zeros(cap_me, self.k, device=dev, dtype=dt)
         self.out = torch.zeros(self.a_local, self.n, device=dev, dtype=dt)
         self.barrier_word = torch.zeros(1, **i32)
+        # Device barrier: flags[s] = last epoch rank s signalled to this rank;
+        # epoch = barriers this rank has passed (both zero at start).
+        self.sync_flags = torch.zeros(world, **i32)
+        self.epoch = torch.zeros(1, **i32)
         self._peer_bases = {}
         if exchange:
             self.set_peer_pointers(*self._exchange_pointers(lib))
 
-    def set_peer_pointers(self, xpk, outs):
-        """Per-rank device pointers of the packed-input and output buffers."""
+    def shared_buffers(self):
+        """The buffers peers write into, in pointer-exchange order."""
+        return (self.x_packed, self.out, self.ids_global, self.sync_flags)
+
+    def set_peer_pointers(self, xpk, outs, ids=None, flags=None):
+        """Per-rank device pointers of the packed-input, output, id-table and
+        barrier-flag buffers (the last two only for ``sync="device"``)."""
         if len(xpk) != self.world or len(outs) != self.world:
             raise ValueError("one pointer per rank")
         self.xpk_ptrs = _ptr_array(xpk, self.device)
         self.out_ptrs = _ptr_array(outs, self.device)
+        if ids is not None:
+            self.ids_ptrs = _ptr_array(ids, self.device)
+        if flags is not None:
+            self.flag_ptrs = _ptr_array(flags, self.device)
 
     def _exchange_pointers(self, lib):
-        """Per-rank device pointers of every rank's packed and output buffers."""
+        """Per-rank device pointers of every rank's shared buffers."""
         import torch.distributed as dist
 
         mine = []
-        for t in (self.x_packed, self.out):
+        for t in self.shared_buffers():
             handle = ctypes.create_string_buffer(64)
             offset = ctypes.c_int64(0)
             if self.world > 1:
@@ -420,12 +472,11 @@ class PeerExpertParallelMoE:
             dist.all_gather_object(every, mine, group=self.group)
         else:
             every = [mine]
-        xpk, outs = [], []
+        per_buffer = [[] for _ in self.shared_buffers()]
         for r in range(self.world):
-            ptrs = []
-            for i, t in enumerate((self.x_packed, self.out)):
+            for i, t in enumerate(self.shared_buffers()):
                 if r == self.rank:
-                    ptrs.append(t.data_ptr())
+                    per_buffer[i].append(t.data_ptr())
                     continue
                 handle, offset = every[r][i]
                 base = self._peer_bases.get(handle)
@@ -434,10 +485,8 @@ class PeerExpertParallelMoE:
                     _native.check(lib.bokt_ipc_import(handle, 0, ctypes.byref(b),
                                                       ctypes.byref(p)), "bokt_ipc_import")
                     base = self._peer_bases[handle] = b.value
-                ptrs.append(base + offset)
-            xpk.append(ptrs[0])
-            outs.append(ptrs[1])
-        return xpk, outs
+                per_buffer[i].append(base + offset)
+        return per_buffer
 
     def close(self):
         """Unmap the peers' buffers (after the last step has completed everywhere)."""
@@ -447,18 +496,36 @@ class PeerExpertParallelMoE:
         self._peer_bases = {}
 
     def _barrier(self):
-        import torch.distributed as dist
+        if self.world == 1 or self.sync == "none":
+            return
+        if self.sync == "nccl":
+            import torch.distributed as dist
 
-        if self.world > 1:
             dist.all_reduce(self.barrier_word, group=self.group)
+            return
+        _native.check(_native.load().bokt_ep_barrier(
+            self.flag_ptrs.data_ptr(), self.epoch.data_ptr(), self.world, self.rank,
+            self.barrier_timeout_ns, _native.current_stream(self.device)), "bokt_ep_barrier")
 
     def _all_gather_ids(self, ids_local):
-        import torch.distributed as dist
-
         if self.world == 1:
             self.ids_global.copy_(ids_local.reshape(-1))
-        else:
+            return
+        if self.sync == "nccl":
+            import torch.distributed as dist
+
             dist.all_gather_into_tensor(self.ids_global, ids_local.reshape(-1), group=self.group)
+            return
+        if self.sync == "none":
+            raise RuntimeError("sync='none': the caller fills ids_global and orders the phases")
+        flat = ids_local.reshape(-1)
+        if flat.numel() != self.a_local or not flat.is_contiguous() or flat.dtype != self.ids_global.dtype:
+            raise ValueError("ids_local must be a contiguous int32 [tokens_per_rank, topk] tensor")
+        _native.check(_native.load().bokt_ep_put(
+            flat.data_ptr(), self.a_local * 4, self.ids_ptrs.data_ptr(),
+            self.rank * self.a_local * 4, self.world, _native.current_stream(self.device)),
+            "bokt_ep_put")
+        self._barrier()
 
     def layout(self):
         """Global routing, per-step layout and this rank's row map."""
@@ -499,14 +566,22 @@ class PeerExpertParallelMoE:
             self.out_ptrs.data_ptr(), self.a_local, self.world, ctypes.byref(self.params),
             _native.current_stream(self.device)), "bokt_moe_grouped_gemm_scatter")
 
-    def forward(self, x_local, ids_local):
+    def forward(self, x_local, ids_local, check=False):
         """x_local [tokens_per_rank, K], ids_local [tokens_per_rank, topk] int32 ->
         [tokens_per_rank * topk, N] (this rank's output buffer, overwritten by
-        the next step): row t*topk + k = x[t] @ W[ids[t, k]]."""
+        the next step): row t*topk + k = x[t] @ W[ids[t, k]].
+
+        ``check=True`` synchronises after the step and raises RuntimeError if a
+        kernel recorded a failure (ids out of range, a packed buffer too small
+        for this routing, a barrier timeout); without it the step never
+        synchronises (graph-capturable) and failures stay in the device status
+        word (``_native.device_status``)."""
         self._all_gather_ids(ids_local)
         self.layout()
         self.dispatch(x_local)
         self._barrier()
         self.compute_and_combine()
         self._barrier()
+        if check:
+            check_device_status(f"expert-parallel step on rank {self.rank}")
         return self.out

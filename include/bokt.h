@@ -353,6 +353,28 @@ int bokt_ep_rowmap(const int32_t* perm, const int32_t* ids, const int32_t* offse
                    int E, int me, int capacity, int32_t* rowmap, void* stream);
 
 /*
+ * Expert-parallel step synchronisation without a host collective (plain
+ * NVLink peer loads and stores; each rank on its own GPU).
+ * bokt_ep_put: copies `bytes` from src into dst_ptrs[d] + dst_offset_bytes for
+ * every rank d (dst_ptrs: device array of `world` pointers, peers' buffers
+ * mapped through CUDA IPC); 16-byte aligned sizes and offsets.  The
+ * all-gather of the routing ids.
+ * bokt_ep_barrier: every rank advances the device counter `epoch` (its own
+ * memory, zero-initialised) and stores the new epoch into slot `me` of every
+ * rank's flag array flag_ptrs[d] (int32[world] per rank, zero-initialised,
+ * peers' through CUDA IPC); then waits until every slot of flag_ptrs[me] has
+ * reached the epoch.  All ranks must call the same sequence of barriers.  A
+ * wait longer than timeout_ns records a timeout in the device status word
+ * (detail 4000 + the silent rank) and returns.  Capturable in a CUDA graph
+ * (the epoch lives on the device).  No counterpart in the reference (its
+ * worker runs one GPU).
+ */
+int bokt_ep_put(const void* src, int64_t bytes, void* const* dst_ptrs, int64_t dst_offset_bytes,
+                int world, void* stream);
+int bokt_ep_barrier(int32_t* const* flag_ptrs, int32_t* epoch, int world, int me,
+                    int64_t timeout_ns, void* stream);
+
+/*
  * CUDA IPC plumbing for the expert-parallel peer buffers.  bokt_ipc_export
  * writes the 64-byte IPC handle of the allocation containing `ptr` and the
  * offset of `ptr` inside it (works for sub-allocations of a caching

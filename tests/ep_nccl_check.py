@@ -1,8 +1,11 @@
 """torchrun worker for tests/test_gpu_expert_parallel.py::test_nccl_two_ranks.
 
 Each rank owns a block of tokens, holds only its virtual experts' weights, and
-runs ExpertParallelMoE.forward with NCCL all-gather / all-to-all.  Rank outputs
-are checked against x[token] @ W[expert] (fp32) with the reference gate.
+runs ExpertParallelMoE.forward with NCCL all-gather / all-to-all, then the
+peer-memory path with device barriers (eager, and captured in a CUDA graph)
+and with NCCL barriers, and a step whose routing differs from the plan.  Rank
+outputs are checked against x[token] @ W[expert] (fp32) with the reference
+gate and must be bit-identical across the paths.
 """
 
 import os
@@ -47,16 +50,44 @@ def main():
     a = np.arange(rank * tpr * 2, (rank + 1) * tpr * 2)
     ref = np.einsum("ak,akn->an", x.float().numpy()[a // 2], w.float().numpy()[ids[a]])
     stats = numerics.check_output(out.float().cpu().numpy(), ref, "bf16")
-    # Peer-memory path (CUDA IPC + NVLink stores, one-word NCCL barriers).
-    pm = ep.PeerExpertParallelMoE(lw, placement, plan, rank, world, 2, tpr)
+    xl = x[rank * tpr:(rank + 1) * tpr].to(device)
+    results = {}
+    # Peer-memory path (CUDA IPC + NVLink stores), device barriers and NCCL barriers.
+    for sync in ("device", "nccl"):
+        pm = ep.PeerExpertParallelMoE(lw, placement, plan, rank, world, 2, tpr, sync=sync)
+        for _ in range(2):
+            pout = pm.forward(xl, ids_local, check=True)
+        torch.cuda.synchronize()
+        results[sync] = (pout.clone(), pm)
+    # The device-barrier step captured in a CUDA graph (no host collective inside).
+    pm = results["device"][1]
+    stream = torch.cuda.Stream(device)
+    graph = torch.cuda.CUDAGraph()
+    dist.barrier()
+    with torch.cuda.graph(graph, stream=stream):
+        for _ in range(3):
+            pm.forward(xl, ids_local)
     for _ in range(2):
-        pout = pm.forward(x[rank * tpr:(rank + 1) * tpr].to(device), ids_local)
+        graph.replay()
+    torch.cuda.synchronize()
+    gout = pm.out.clone()
+    del graph
+    ep.check_device_status("graph replay")
+    # A routing the plan was not made for (all tokens on experts 0 and 1).
+    other = torch.tensor([[0, 1]] * tpr, dtype=torch.int32, device=device).reshape(-1)
+    oout = pm.forward(xl, other, check=True).clone()
     torch.cuda.synchronize()
     code2, _ = _native.device_status(reset=True)
-    pstats = numerics.check_output(pout.float().cpu().numpy(), ref, "bf16")
-    same = bool(torch.equal(pout, out))
+    pstats = numerics.check_output(results["device"][0].float().cpu().numpy(), ref, "bf16")
+    oa = np.arange(rank * tpr * 2, (rank + 1) * tpr * 2)
+    oids = np.tile([0, 1], tpr)
+    oref = np.einsum("ak,akn->an", x.float().numpy()[oa // 2], w.float().numpy()[oids])
+    ostats = numerics.check_output(oout.float().cpu().numpy(), oref, "bf16")
+    same = bool(torch.equal(results["device"][0], out) and torch.equal(results["nccl"][0], out)
+                and torch.equal(gout, out))
     dist.barrier()
-    pm.close()
+    for _, m in results.values():
+        m.close()
     code = code or code2
     ok = torch.tensor([1 if code == 0 and same else 0], device=device)
     dist.all_reduce(ok, op=dist.ReduceOp.MIN)
@@ -64,8 +95,9 @@ def main():
     dist.destroy_process_group()
     if rank == 0 and ok.item() == 1:
         print(f"EP_NCCL_OK rel={stats['normwise_rel_error']:.2e} "
-              f"peer rel={pstats['normwise_rel_error']:.2e} identical={same}")
-    return 0 if code == 0 else 1
+              f"peer rel={pstats['normwise_rel_error']:.2e} other-routing "
+              f"rel={ostats['normwise_rel_error']:.2e} identical={same}")
+    return 0 if ok.item() == 1 else 1
 
 
 if __name__ == "__main__":

@@ -127,6 +127,9 @@ def test_single_rank_forward_matches_one_gpu_path(cuda_device):
 
 
 def test_nccl_two_ranks(cuda_device):
+    """Real ranks on two GPUs: the NCCL path, the peer path with device
+    barriers (eager and captured in a CUDA graph) and with NCCL barriers, a
+    routing that differs from the plan; all results identical and exact."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs for a real NCCL run; the virtual-rank test covers one GPU")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
@@ -140,7 +143,7 @@ def test_nccl_two_ranks(cuda_device):
 
 
 def build_peer_ranks(world, tokens, experts, k, n, seed, device, dtype=torch.bfloat16,
-                     params=None):
+                     params=None, capacity="worst"):
     ids_cpu = zipf_routing(tokens, experts, 2, 1.1, seed).reshape(-1)
     ids = ids_cpu.numpy()
     placement = ep.plan_placement(np.bincount(ids, minlength=experts), world)
@@ -152,7 +155,7 @@ def build_peer_ranks(world, tokens, experts, k, n, seed, device, dtype=torch.bfl
     wd = w.to(device)
     ranks = [ep.PeerExpertParallelMoE(wd[ep.local_weight_slices(placement, r)].contiguous(),
                                       placement, plan, r, world, 2, tpr, params=params,
-                                      exchange=False)
+                                      exchange=False, capacity=capacity)
              for r in range(world)]
     xpk = [m.x_packed.data_ptr() for m in ranks]
     outs = [m.out.data_ptr() for m in ranks]
@@ -207,3 +210,92 @@ def test_peer_path_single_rank_forward(cuda_device):
     torch.cuda.synchronize()
     a = np.arange(tokens * 2)
     gate(out, np.einsum("ak,akn->an", as_f32(x)[a // 2], as_f32(w)[ids[a]]), "bf16")
+
+
+def run_peer_phases(ranks, ids_dev, xd, tpr):
+    """One peer-path step of ranks sharing this GPU: each phase for every rank
+    in turn (stream order stands in for the device barriers)."""
+    for m in ranks:
+        m.out.fill_(float("nan"))
+        m.ids_global.copy_(ids_dev)
+        m.layout()
+    for r, m in enumerate(ranks):
+        m.dispatch(xd[r * tpr:(r + 1) * tpr])
+    for m in ranks:
+        m.compute_and_combine()
+
+
+@pytest.mark.parametrize("capacity", ["worst", "plan"])
+def test_peer_path_routing_differs_from_plan(capacity, cuda_device):
+    """The placement comes from one routing, the step sees another that piles
+    every token on experts 0 and 1.  With worst-case capacity (the default) the
+    result is still exact; with plan-sized buffers the overflow is reported
+    (status 4) instead of silently dropping rows, and forward-style checking
+    raises."""
+    world, tokens, experts, k, n = 4, 2048, 16, 128, 256
+    ids_cpu, ids, x, w, placement, ranks = build_peer_ranks(world, tokens, experts, k, n, 21,
+                                                            cuda_device, capacity=capacity)
+    step_ids = torch.tensor([[0, 1]] * tokens, dtype=torch.int32).reshape(-1)
+    tpr = tokens // world
+    _native.device_status(reset=True)
+    run_peer_phases(ranks, step_ids.to(cuda_device), x.to(cuda_device), tpr)
+    torch.cuda.synchronize()
+    if capacity == "plan":
+        with pytest.raises(RuntimeError, match="too small"):
+            ep.check_device_status("step")
+        return
+    ep.check_device_status("step")
+    xf, wf, sid = as_f32(x), as_f32(w), step_ids.numpy()
+    for r, m in enumerate(ranks):
+        a = np.arange(r * tpr * 2, (r + 1) * tpr * 2)
+        gate(m.out, np.einsum("ak,akn->an", xf[a // 2], wf[sid[a]]), "bf16")
+
+
+def _ptrs(tensors, device):
+    return torch.tensor([t.data_ptr() for t in tensors], dtype=torch.int64, device=device)
+
+
+def test_device_barrier_success_and_timeout(cuda_device):
+    """bokt_ep_barrier as rank 0 of 2, both flag arrays in this GPU's memory.
+    First call: the peer never signals -> the wait gives up after 50 ms,
+    records status 1 with detail 4001 (rank 1) and returns; this rank's signal
+    reached both arrays.  Second call with the peer's signal already in place:
+    passes with no status.  A GEMM right after runs normally."""
+    lib = _native.load()
+    stream = _native.current_stream(cuda_device)
+    mine = torch.zeros(2, dtype=torch.int32, device=cuda_device)
+    peer = torch.zeros(2, dtype=torch.int32, device=cuda_device)
+    epoch = torch.zeros(1, dtype=torch.int32, device=cuda_device)
+    ptrs = _ptrs([mine, peer], cuda_device)
+    _native.device_status(reset=True)
+    _native.check(lib.bokt_ep_barrier(ptrs.data_ptr(), epoch.data_ptr(), 2, 0, 50_000_000,
+                                      stream), "barrier")
+    assert _native.device_status(reset=True) == (1, 4001)
+    assert epoch.item() == 1 and mine[0].item() == 1 and peer[0].item() == 1
+    mine[1] = 2  # rank 1 has already reached barrier 2
+    _native.check(lib.bokt_ep_barrier(ptrs.data_ptr(), epoch.data_ptr(), 2, 0, 50_000_000,
+                                      stream), "barrier")
+    assert _native.device_status(reset=True) == (0, 0)
+    assert epoch.item() == 2 and peer[0].item() == 2
+    a = torch.randn(256, 384, device=cuda_device).bfloat16()
+    b = torch.randn(384, 512, device=cuda_device).bfloat16()
+    from flashattentionanycard_b200.kernels import gemm
+    out = torch.empty(256, 512, device=cuda_device, dtype=torch.bfloat16)
+    gemm.launch(a, b, out, {})
+    torch.cuda.synchronize()
+    gate(out, as_f32(a.cpu()) @ as_f32(b.cpu()), "bf16")
+
+
+def test_put_copies_into_every_rank(cuda_device):
+    lib = _native.load()
+    world, chunk = 3, 96
+    src = torch.arange(chunk, dtype=torch.int32, device=cuda_device) + 7
+    dsts = [torch.full((world * chunk,), -1, dtype=torch.int32, device=cuda_device)
+            for _ in range(world)]
+    _native.check(lib.bokt_ep_put(src.data_ptr(), chunk * 4, _ptrs(dsts, cuda_device).data_ptr(),
+                                  1 * chunk * 4, world, _native.current_stream(cuda_device)),
+                  "put")
+    torch.cuda.synchronize()
+    for d in dsts:
+        assert torch.equal(d[chunk:2 * chunk], src)
+        assert int(d[:chunk].max()) == -1 and int(d[2 * chunk:].max()) == -1
