@@ -339,20 +339,32 @@ def moe_large_placement(cfg, world):
     return ids, placement
 
 
+def moe_large_gates(cfg):
+    """Gate weights of the top-k experts per token: seeded, positive, each
+    token's weights summing to 1 (fp32 [tokens, topk])."""
+    import torch
+
+    g = torch.Generator().manual_seed(2)
+    raw = torch.rand(cfg["tokens"], cfg["topk"], generator=g) + 0.25
+    return (raw / raw.sum(1, keepdim=True)).contiguous()
+
+
 def moe_large_config(world):
     c = moe_large_cfg()
     out = {"workload": f"moe_bf16_E{c['experts']}_K{c['k']}_N{c['n']}_T{c['tokens']}_top2_zipf1.1",
            "partition": "single GPU (all experts local)",
-           "step": "route + gather + grouped GEMM", "l2": "W 7.5 GB > L2",
+           "step": "route + gather + grouped GEMM + gate-weighted combine (MoE layer; FLOPs "
+                   "counted: the grouped GEMM)", "l2": "W 7.5 GB > L2",
            "params": params_for("moe_grouped_gemm")}
     if world > 1:
         _, p = moe_large_placement(c, world)
         step = ("ids put to every rank + device barrier + route + NVLink peer-store dispatch "
-                "+ device barrier + grouped GEMM with peer-store combine epilogue + device "
-                "barrier; no host collective, steps captured in CUDA graphs"
+                "+ device barrier + grouped GEMM with peer-store epilogue (rows to their token "
+                "owners) + device barrier with the gate-weighted combine fused in; no host "
+                "collective, steps captured in CUDA graphs"
                 if EP_COMM == "peer" else
                 "all-gather ids + route + dispatch all-to-all + grouped GEMM + "
-                "combine all-to-all (NCCL), eager")
+                "return all-to-all (NCCL) + gate-weighted combine, eager")
         out.update({
             "partition": f"expert-parallel over {world} GPUs: {p.virtual_experts} virtual "
                          f"experts (hot experts replicated, rows split), LPT placement",
@@ -736,10 +748,12 @@ class MoeLarge:
         self.world, self.rank = world, rank
         self.params = params_for("moe_grouped_gemm")
         self.kernel, gemm_launches = grouped_kernel_label(self.params)
-        self.launches_per_step = 4 + gemm_launches  # route: count, scan, scatter; gather; GEMM
+        # route: count, scan, scatter; gather; GEMM; combine
+        self.launches_per_step = 5 + gemm_launches
         self.x, self.w, ids = workloads.moe_large_inputs("bf16", seed=0, device=device,
                                                          experts=cfg["experts"])
         self.ids_cpu = ids
+        self.gates_cpu = moe_large_gates(cfg)
         self.sm = torch.cuda.get_device_properties(device).multi_processor_count
         a = ids.numel()
         self.flops_per_step = 2.0 * a * cfg["k"] * cfg["n"]  # whole job, all ranks
@@ -748,9 +762,11 @@ class MoeLarge:
             self._init_expert_parallel(ids, device)
             return
         self.ids = ids.reshape(-1).to(device)
+        self.gates = self.gates_cpu.to(device)
         self.router = MoeRouter(a, cfg["experts"], device)
         self.packed = torch.empty(a, cfg["k"], device=device, dtype=torch.bfloat16)
         self.y = torch.empty(a, cfg["n"], device=device, dtype=torch.bfloat16)
+        self.final = torch.empty(cfg["tokens"], cfg["n"], device=device, dtype=torch.bfloat16)
 
     def _init_expert_parallel(self, ids, device):
         import numpy as np
@@ -773,13 +789,14 @@ class MoeLarge:
         del self.x
         self.ids_local = ids.reshape(-1)[rank * tpr * cfg["topk"]:(rank + 1) * tpr * cfg["topk"]]
         self.ids_local = self.ids_local.to(torch.int32).to(device)
+        self.gates_local = self.gates_cpu[rank * tpr:(rank + 1) * tpr].contiguous().to(device)
         self.comm = EP_COMM
         if self.comm == "peer":
             self.ep = ep.PeerExpertParallelMoE(local, self.placement, self.plan, rank, world,
                                                cfg["topk"], tpr, group=dist.group.WORLD,
                                                params=self.params, sm_count=self.sm)
-            # put, 3 barriers, route x3, plan, rowmap, dispatch, grouped GEMM with the
-            # peer-scatter epilogue
+            # put, 2 barriers, route x3, plan, rowmap, dispatch, grouped GEMM with the
+            # peer-scatter epilogue, barrier with the fused combine
             label, gemm_launches = grouped_kernel_label(self.params)
             self.kernel = label.replace(",grouped", ",grouped,scatter")
             self.launches_per_step = 10 + gemm_launches
@@ -787,8 +804,8 @@ class MoeLarge:
             self.ep = ep.ExpertParallelMoE(local, self.placement, self.plan, rank, world,
                                            cfg["topk"], tpr, group=dist.group.WORLD,
                                            params=self.params, sm_count=self.sm)
-            # routing/keys/sorts/checks + 4 gathers + grouped GEMM
-            self.launches_per_step = 20 + grouped_kernel_label(self.params)[1]
+            # routing/keys/sorts/checks + 4 gathers + grouped GEMM + combine
+            self.launches_per_step = 21 + grouped_kernel_label(self.params)[1]
         torch.cuda.empty_cache()
         # Peer path: device barriers only, so whole steps are captured in CUDA
         # graphs.  NCCL path: host collectives between kernels, timed eagerly.
@@ -799,16 +816,36 @@ class MoeLarge:
         self.expected_local_rows = np.asarray(self.plan.local_rows[rank], dtype=np.int64)
 
     def step(self, i):
-        from flashattentionanycard_b200.kernels import moe_grouped_gemm
-        from flashattentionanycard_b200.kernels.moe_routing import gather_rows
-
         if self.world > 1:
-            self.ep.forward(self.x_local, self.ids_local)
+            self.ep_step(self.x_local, self.ids_local, self.gates_local)
             return
-        self.router(self.ids)
-        gather_rows(self.x, self.router.perm, self.packed, divisor=self.cfg["topk"])
+        self.layer(self.x, self.ids, self.gates, self.final)
+
+    def layer(self, x, ids, gates, final):
+        """One GPU: route -> gather -> grouped GEMM -> gate-weighted combine."""
+        from flashattentionanycard_b200.kernels import moe_grouped_gemm
+        from flashattentionanycard_b200.kernels.moe_routing import combine, gather_rows
+
+        self.router(ids)
+        gather_rows(x, self.router.perm, self.packed, divisor=self.cfg["topk"])
         moe_grouped_gemm.launch(self.packed, self.w, self.router.offsets, self.y, self.params,
                                 self.sm)
+        combine(self.y, gates, final, self.router.inv_perm)
+
+    def ep_step(self, x_local, ids_local, gates_local):
+        """N GPUs: the expert-parallel step, returning the token-order layer output."""
+        from flashattentionanycard_b200.kernels.moe_routing import combine
+
+        if self.comm == "peer":
+            return self.ep.forward(x_local, ids_local, gates_local)
+        out = self.ep.forward(x_local, ids_local)
+        if not hasattr(self, "final_local"):
+            import torch
+
+            self.final_local = torch.empty(out.shape[0] // self.cfg["topk"], out.shape[1],
+                                           device=out.device, dtype=out.dtype)
+        combine(out, gates_local, self.final_local)
+        return self.final_local
 
     def dominant_kernel(self, i):  # noqa: ARG002 - same inputs every launch
         from flashattentionanycard_b200.kernels import moe_grouped_gemm
@@ -826,54 +863,58 @@ class MoeLarge:
         return self.flops_per_step / seconds_per_step / 1e12  # whole job at any world size
 
     def parity(self):
+        """Sampled tokens of the layer output (token order, gate-weighted
+        combine of the top-k expert rows) against x[t] @ W[e] in fp32 on the
+        device, on the first and last 256 output columns; routing bit-exact."""
         import numpy as np
         import torch
 
         topk = self.cfg["topk"]
+        self.step(0)
+        torch.cuda.synchronize()
+        flat = self.ids_cpu.reshape(-1).numpy()
+        cols = list(range(256)) + list(range(self.cfg["n"] - 256, self.cfg["n"]))
         if self.world == 1:
-            self.step(0)
-            torch.cuda.synchronize()
-            flat = self.ids_cpu.reshape(-1).numpy()
             exact = bool(np.array_equal(self.router.counts.cpu().numpy(),
                                         np.bincount(flat, minlength=self.cfg["experts"])))
             exact = exact and bool(np.array_equal(self.router.perm.cpu().numpy(),
                                                   np.argsort(flat, kind="stable")))
-            rows = sample_rows(self.y.shape[0], 32)
-            perm = self.router.perm.cpu()
-            x_rows = self.x[(perm[rows] // topk).to(self.x.device)]
-            xs = torch.zeros_like(self.packed)
-            xs[rows] = x_rows
-            out = grouped_parity(xs, self.w, self.router.offsets, self.y, rows)
-            out["ok"] = out["ok"] and exact
-            out["routing_counts_exact"] = exact
-            out["checked"] = (f"{len(rows)} sampled packed rows x {self.cfg['n']} columns; "
-                              "expert counts and the permutation bit-exact vs numpy "
-                              "bincount / stable argsort")
-            return out
-        self.step(0)
-        torch.cuda.synchronize()
-        ep = self.ep
-        route = ep.route_global if hasattr(ep, "route_global") else None
-        exact = route is not None and bool(np.array_equal(route.counts.cpu().numpy(),
-                                                           self.expected_counts))
-        if self.comm == "peer":
-            lrows = np.diff(ep.loffs.cpu().numpy().astype(np.int64))
-            exact = exact and bool(np.array_equal(lrows, self.expected_local_rows))
-        out_rows = ep.out
-        rows = sample_rows(out_rows.shape[0], 32, seed=self.rank)
-        ids = self.ids_local.reshape(-1).cpu()
-        cols = self.check_cols
-        refs, outs = [], []
-        for r in rows:
-            e = int(ids[r])
-            refs.append(self.x_local[r // topk:r // topk + 1].float() @ self.w_cols[e].float())
-            outs.append(out_rows[r:r + 1, cols])
-        res = gate_check(torch.cat(outs), torch.cat(refs), "bf16")
+            final, x_tok, first = self.final, self.x, 0
+            what = "expert counts and the permutation bit-exact vs numpy bincount / stable argsort"
+
+            def w_cols(e):
+                return self.w[e][:, cols]
+        else:
+            ep = self.ep
+            exact = bool(np.array_equal(ep.route_global.counts.cpu().numpy(),
+                                        self.expected_counts))
+            if self.comm == "peer":
+                lrows = np.diff(ep.loffs.cpu().numpy().astype(np.int64))
+                exact = exact and bool(np.array_equal(lrows, self.expected_local_rows))
+                final = ep.final
+            else:
+                final = self.final_local
+            x_tok = self.x_local
+            first = self.rank * x_tok.shape[0]
+            what = ("global expert counts and local rows per virtual expert bit-exact vs the "
+                    "host plan")
+
+            def w_cols(e):
+                return self.w_cols[e]
+        tokens = sample_rows(final.shape[0], 32, seed=self.rank)
+        refs = []
+        for t in tokens:
+            acc = torch.zeros(1, len(cols), device=final.device)
+            for j in range(topk):
+                e = int(flat[(first + t) * topk + j])
+                g = float(self.gates_cpu[first + t, j])
+                acc += g * (x_tok[t:t + 1].float() @ w_cols(e).float())
+            refs.append(acc)
+        res = gate_check(final[tokens][:, cols], torch.cat(refs), "bf16")
         res["ok"] = res["ok"] and exact
-        res["plan_counts_exact"] = exact
-        res["checked"] = (f"rank {self.rank}: {len(rows)} sampled output rows x {len(cols)} "
-                          "columns (first and last 256); global expert counts and local rows "
-                          "per virtual expert bit-exact vs the host plan")
+        res["routing_exact"] = exact
+        res["checked"] = (f"rank {self.rank}: {len(tokens)} sampled tokens of the layer output "
+                          f"x {len(cols)} columns (first and last 256); {what}")
         return res
 
     def e2e_setup(self):
@@ -882,34 +923,36 @@ class MoeLarge:
         if self.world > 1:
             self.hx = self.x_local.cpu().pin_memory()
             self.hids = self.ids_local.cpu().pin_memory()
-            self.hy = torch.empty(self.ep.out.shape, dtype=self.ep.out.dtype).pin_memory()
+            self.hg = self.gates_local.cpu().pin_memory()
+            rows = self.x_local.shape[0]
+            self.hy = torch.empty(rows, self.cfg["n"], dtype=torch.bfloat16).pin_memory()
             self.dx, self.dids = torch.empty_like(self.x_local), torch.empty_like(self.ids_local)
-            self.h2d = self.hx.numel() * 2 + self.hids.numel() * 4
+            self.dg = torch.empty_like(self.gates_local)
+            self.h2d = self.hx.numel() * 2 + self.hids.numel() * 4 + self.hg.numel() * 4
             self.d2h = self.hy.numel() * 2
             return
-        self.h_in = [self.x.cpu().pin_memory(), self.ids.cpu().pin_memory()]
-        self.d_in = [[torch.empty_like(self.x), torch.empty_like(self.ids)] for _ in range(2)]
-        self.d_out = [self.y, torch.empty_like(self.y)]
-        self.h_out = [torch.empty(self.y.shape, dtype=self.y.dtype).pin_memory() for _ in range(2)]
+        self.h_in = [self.x.cpu().pin_memory(), self.ids.cpu().pin_memory(),
+                     self.gates.cpu().pin_memory()]
+        self.d_in = [[torch.empty_like(t, device=self.x.device) for t in self.h_in]
+                     for _ in range(2)]
+        self.d_out = [self.final, torch.empty_like(self.final)]
+        self.h_out = [torch.empty(self.final.shape, dtype=self.final.dtype).pin_memory()
+                      for _ in range(2)]
         self.h2d = sum(t.numel() * t.element_size() for t in self.h_in)
         self.d2h = self.h_out[0].numel() * 2
 
     def e2e_step(self):
-        """Expert-parallel step with its host copies (collectives inside: not pipelined)."""
+        """Expert-parallel step with its host copies (not pipelined)."""
         self.dx.copy_(self.hx, non_blocking=True)
         self.dids.copy_(self.hids, non_blocking=True)
-        out = self.ep.forward(self.dx, self.dids)
+        self.dg.copy_(self.hg, non_blocking=True)
+        out = self.ep_step(self.dx, self.dids, self.dg)
         self.hy.copy_(out, non_blocking=True)
 
     def e2e_compute(self, b):
-        from flashattentionanycard_b200.kernels import moe_grouped_gemm
-        from flashattentionanycard_b200.kernels.moe_routing import gather_rows
-
-        x, ids = self.d_in[b]
-        self.router(ids)  # one routing state: the compute stream orders consecutive steps
-        gather_rows(x, self.router.perm, self.packed, divisor=self.cfg["topk"])
-        moe_grouped_gemm.launch(self.packed, self.w, self.router.offsets, self.d_out[b],
-                                self.params, self.sm)
+        x, ids, gates = self.d_in[b]
+        # One routing state: the compute stream orders consecutive steps.
+        self.layer(x, ids, gates, self.d_out[b])
 
     def release(self):
         """Unmap the peers' buffers (every rank, after a barrier)."""

@@ -111,6 +111,8 @@ SIGNATURES = {
     "bokt_ep_rowmap": (_I32, [_VP] * 9 + [_I32] * 4 + [_VP, _VP]),
     "bokt_ep_put": (_I32, [_VP, _I64, _VP, _I64, _I32, _VP]),
     "bokt_ep_barrier": (_I32, [_VP, _VP, _I32, _I32, _I64, _VP]),
+    "bokt_ep_barrier_combine": (
+        _I32, [_VP, _VP, _I32, _I32, _I64, _VP, _VP, _VP, _I32, _I32, _I32, _I32, _VP]),
     "bokt_ipc_export": (_I32, [_VP, _VP, ctypes.POINTER(ctypes.c_int64)]),
     "bokt_ipc_import": (_I32, [_VP, _I64, ctypes.POINTER(_VP), ctypes.POINTER(_VP)]),
     "bokt_ipc_close": (_I32, [_VP]),

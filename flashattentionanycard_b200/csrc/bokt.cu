@@ -844,6 +844,43 @@ int bokt_ep_barrier(int32_t* const* flag_ptrs, int32_t* epoch, int world, int me
   return BOKT_OK;
 }
 
+int bokt_ep_barrier_combine(int32_t* const* flag_ptrs, int32_t* epoch, int world, int me,
+                            int64_t timeout_ns, const void* y, const float* gates, void* out,
+                            int tokens, int k, int N, int dtype, void* stream) {
+  g_err[0] = 0;
+  if (world <= 0 || world > bokt::kEpMaxWorld || me < 0 || me >= world)
+    return fail(BOKT_ERR_INVALID, "bad world/rank");
+  if (timeout_ns <= 0 || timeout_ns > 60000000000ll)
+    return fail(BOKT_ERR_INVALID, "timeout must be in (0, 60 s]");
+  if (dtype != BOKT_FP16 && dtype != BOKT_BF16) return fail(BOKT_ERR_INVALID, "dtype %d", dtype);
+  if (tokens < 0 || k <= 0 || N <= 0) return fail(BOKT_ERR_INVALID, "bad size");
+  if (!flag_ptrs || !epoch || (tokens > 0 && (!y || !gates || !out)))
+    return fail(BOKT_ERR_INVALID, "null pointer");
+  if (N % 8 != 0 || (tokens > 0 && (!aligned16(y) || !aligned16(out))))
+    return fail(BOKT_ERR_UNSUPPORTED, "combine needs N %% 8 == 0 and 16-byte aligned rows");
+  DeviceInfo dev;
+  int rc = device_info(&dev);
+  if (rc) return rc;
+  // Every CTA waits for the peers, so keep the grid within one wave.
+  long long grid = tokens < 1 ? 1 : tokens;
+  if (grid > 4LL * dev.sm_count) grid = 4LL * dev.sm_count;
+  const int threads = N / 8 < 256 ? ((N / 8 + 31) / 32) * 32 : 256;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const long long y_rows = (long long)tokens * k;
+  cudaError_t e =
+      dtype == BOKT_BF16
+          ? launch(bokt::ep_barrier_combine_kernel<__nv_bfloat16>, dim3(unsigned(grid)),
+                   dim3(threads), 0, s, flag_ptrs, epoch, world, me, (long long)timeout_ns,
+                   static_cast<const __nv_bfloat16*>(y), y_rows, gates,
+                   static_cast<__nv_bfloat16*>(out), tokens, k, N)
+          : launch(bokt::ep_barrier_combine_kernel<__half>, dim3(unsigned(grid)), dim3(threads),
+                   0, s, flag_ptrs, epoch, world, me, (long long)timeout_ns,
+                   static_cast<const __half*>(y), y_rows, gates, static_cast<__half*>(out),
+                   tokens, k, N);
+  if (e != cudaSuccess) return cuda_fail(e, "ep_barrier_combine launch");
+  return BOKT_OK;
+}
+
 int bokt_ep_rowmap(const int32_t* perm, const int32_t* ids, const int32_t* offsets,
                    const int32_t* counts, const int32_t* replicas, const int32_t* vbase,
                    const int32_t* v_rank, const int32_t* v_plo, const int32_t* v_lbase, int A,

@@ -23,6 +23,7 @@
 #pragma once
 
 #include "bokt_device.cuh"
+#include "ep_sync.cuh"
 
 namespace bokt {
 
@@ -473,6 +474,50 @@ __global__ void __launch_bounds__(256) moe_topk_gate_kernel(const T* __restrict_
   }
 }
 
+// out[t] = sum_j gates[t k + j] * y[row(t k + j)] for one token, fp32 FMAs in
+// slot order j = 0..k-1, 16-byte vectors spread over the CTA's threads;
+// row(a) = rows[a] when rows is given, else a.  Rows outside [0, y_rows) set
+// *bad and are skipped.
+template <typename T>
+__device__ __forceinline__ void combine_token(const T* __restrict__ y, long long y_rows,
+                                              const int32_t* __restrict__ rows,
+                                              const float* __restrict__ gates,
+                                              T* __restrict__ out, int t, int k, int N,
+                                              bool* bad) {
+  const int nvec = N / 8;
+  const uint4* yv4 = reinterpret_cast<const uint4*>(y);
+  for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+    for (int j = 0; j < k; ++j) {
+      const int a = t * k + j;
+      const long long r = rows ? static_cast<long long>(rows[a]) : static_cast<long long>(a);
+      if (r < 0 || r >= y_rows) {
+        *bad = true;
+        continue;
+      }
+      const float g = gates[a];
+      const uint4 yv = yv4[r * nvec + v];
+      const float2 f0 = Pack2<T>::unpack(yv.x), f1 = Pack2<T>::unpack(yv.y);
+      const float2 f2 = Pack2<T>::unpack(yv.z), f3 = Pack2<T>::unpack(yv.w);
+      acc[0] = fmaf(g, f0.x, acc[0]);
+      acc[1] = fmaf(g, f0.y, acc[1]);
+      acc[2] = fmaf(g, f1.x, acc[2]);
+      acc[3] = fmaf(g, f1.y, acc[3]);
+      acc[4] = fmaf(g, f2.x, acc[4]);
+      acc[5] = fmaf(g, f2.y, acc[5]);
+      acc[6] = fmaf(g, f3.x, acc[6]);
+      acc[7] = fmaf(g, f3.y, acc[7]);
+    }
+    uint4 o;
+    o.x = Pack2<T>::pack(acc[0], acc[1]);
+    o.y = Pack2<T>::pack(acc[2], acc[3]);
+    o.z = Pack2<T>::pack(acc[4], acc[5]);
+    o.w = Pack2<T>::pack(acc[6], acc[7]);
+    reinterpret_cast<uint4*>(out + static_cast<long long>(t) * N)[v] = o;
+  }
+}
+
 // Gate-weighted combine back to token order:
 //   out[t, :] = sum_j gates[t, j] * y[row(t, j), :],  row = rows ? rows[t*k + j] : t*k + j
 // fp32 accumulation, rounded on store; one CTA slice per token, 16-byte vectors.
@@ -484,42 +529,77 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(const T* __restrict__ 
                                                           int N) {
   pdl_allow_next();
   pdl_wait();
-  const int nvec = N / 8;
-  const uint4* yv4 = reinterpret_cast<const uint4*>(y);
   bool bad = false;
-  for (int t = blockIdx.x; t < tokens; t += gridDim.x) {
-    for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll 1
-      for (int j = 0; j < k; ++j) {
-        const int a = t * k + j;
-        const long long r = rows ? static_cast<long long>(rows[a]) : static_cast<long long>(a);
-        if (r < 0 || r >= y_rows) {
-          bad = true;
-          continue;
+  for (int t = blockIdx.x; t < tokens; t += gridDim.x)
+    combine_token(y, y_rows, rows, gates, out, t, k, N, &bad);
+  if (bad) report_status(kStatusBadExpertId, blockIdx.x);
+}
+
+// The expert-parallel step's last barrier with the combine fused into it (the
+// receive side of the peer-store combine).  Every CTA signals this rank's
+// epoch to every rank (flag_ptrs as in ep_barrier_kernel; the stores are
+// idempotent, so no CTA depends on another being scheduled), waits until all
+// ranks have signalled it -- i.e. every peer's grouped GEMM has stored its
+// result rows into this rank's slot buffer y [tokens * k, N] -- and then
+// reduces its share of this rank's tokens: out[t] = sum_j gates[t k + j] *
+// y[t k + j] (combine_token, the arithmetic of moe_combine_kernel).  epoch[0]
+// is the barrier epoch, epoch[1] counts CTAs that finished; the last CTA
+// resets the count and advances the epoch.  On a timeout the CTA records
+// kStatusWaitTimeout (detail 4000 + silent rank) and skips its tokens.
+template <typename T>
+__global__ void __launch_bounds__(256) ep_barrier_combine_kernel(
+    int32_t* const* __restrict__ flag_ptrs, int32_t* __restrict__ epoch, int world, int me,
+    long long timeout_ns, const T* __restrict__ y, long long y_rows,
+    const float* __restrict__ gates, T* __restrict__ out, int tokens, int k, int N) {
+  pdl_allow_next();
+  pdl_wait();
+  __shared__ int32_t s_epoch;
+  __shared__ int s_ok;
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    int32_t e = 0;
+    if (lane == 0) e = epoch[0] + 1;
+    e = __shfl_sync(0xffffffffu, e, 0);
+    __threadfence_system();
+    int ok = 1;
+    if (lane < world) {
+      st_release_sys(flag_ptrs[lane] + me, e);
+      const int32_t* mine = flag_ptrs[me] + lane;
+      const uint64_t start = globaltimer_ns();
+      for (uint32_t it = 0;; ++it) {
+        const uint32_t seen = static_cast<uint32_t>(ld_acquire_sys(mine));
+        if (static_cast<int32_t>(seen - static_cast<uint32_t>(e)) >= 0) break;
+        if ((it & 63u) == 63u &&
+            globaltimer_ns() - start > static_cast<uint64_t>(timeout_ns)) {
+          report_status(kStatusWaitTimeout, 4000 + lane);
+          ok = 0;
+          break;
         }
-        const float g = gates[a];
-        const uint4 yv = yv4[r * nvec + v];
-        const float2 f0 = Pack2<T>::unpack(yv.x), f1 = Pack2<T>::unpack(yv.y);
-        const float2 f2 = Pack2<T>::unpack(yv.z), f3 = Pack2<T>::unpack(yv.w);
-        acc[0] = fmaf(g, f0.x, acc[0]);
-        acc[1] = fmaf(g, f0.y, acc[1]);
-        acc[2] = fmaf(g, f1.x, acc[2]);
-        acc[3] = fmaf(g, f1.y, acc[3]);
-        acc[4] = fmaf(g, f2.x, acc[4]);
-        acc[5] = fmaf(g, f2.y, acc[5]);
-        acc[6] = fmaf(g, f3.x, acc[6]);
-        acc[7] = fmaf(g, f3.y, acc[7]);
       }
-      uint4 o;
-      o.x = Pack2<T>::pack(acc[0], acc[1]);
-      o.y = Pack2<T>::pack(acc[2], acc[3]);
-      o.z = Pack2<T>::pack(acc[4], acc[5]);
-      o.w = Pack2<T>::pack(acc[6], acc[7]);
-      reinterpret_cast<uint4*>(out + static_cast<long long>(t) * N)[v] = o;
+    }
+    ok = __all_sync(0xffffffffu, ok);
+    if (lane == 0) {
+      s_epoch = e;
+      s_ok = ok;
     }
   }
+  __syncthreads();
+  bool bad = false;
+  if (s_ok) {
+    for (int t = blockIdx.x; t < tokens; t += gridDim.x)
+      combine_token(y, y_rows, static_cast<const int32_t*>(nullptr), gates, out, t, k, N, &bad);
+  }
   if (bad) report_status(kStatusBadExpertId, blockIdx.x);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    uint32_t* done = reinterpret_cast<uint32_t*>(epoch + 1);
+    if (atomicAdd(done, 1u) == gridDim.x - 1) {
+      *done = 0;
+      __threadfence();
+      epoch[0] = s_epoch;
+    }
+  }
 }
 
 }  // namespace bokt

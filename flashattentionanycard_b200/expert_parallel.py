@@ -432,9 +432,13 @@ class PeerExpertParallelMoE:
         self.out = torch.zeros(self.a_local, self.n, device=dev, dtype=dt)
         self.barrier_word = torch.zeros(1, **i32)
         # Device barrier: flags[s] = last epoch rank s signalled to this rank;
-        # epoch = barriers this rank has passed (both zero at start).
+        # epoch = [barriers this rank has passed, CTA count of the combining
+        # barrier] (zero at start).
         self.sync_flags = torch.zeros(world, **i32)
-        self.epoch = torch.zeros(1, **i32)
+        self.epoch = torch.zeros(2, **i32)
+        # Token-order result of the combine: final[t] = sum_j g[t, j] out[t topk + j].
+        self.final = torch.empty(tokens_per_rank, self.n, device=dev, dtype=dt)
+        self._own_flag_ptrs = _ptr_array([self.sync_flags.data_ptr()], dev)
         self._peer_bases = {}
         if exchange:
             self.set_peer_pointers(*self._exchange_pointers(lib))
@@ -566,10 +570,41 @@ class PeerExpertParallelMoE:
             self.out_ptrs.data_ptr(), self.a_local, self.world, ctypes.byref(self.params),
             _native.current_stream(self.device)), "bokt_moe_grouped_gemm_scatter")
 
-    def forward(self, x_local, ids_local, check=False):
+    def barrier_combine(self, gates_local):
+        """The step's last barrier with the gate-weighted combine fused into it:
+        once every rank's result rows have landed in this rank's ``out``,
+        final[t] = sum_j gates[t, j] * out[t * topk + j] (fp32, slot order).
+        With ``sync="none"`` (ranks sharing one process) only the combine runs:
+        the caller has already ordered the phases."""
+        import torch
+
+        g = gates_local.reshape(-1)
+        if g.dtype != torch.float32 or g.numel() != self.a_local or not g.is_contiguous():
+            raise ValueError("gates_local must be a contiguous fp32 [tokens_per_rank, topk] tensor")
+        stream = _native.current_stream(self.device)
+        if self.sync == "nccl" and self.world > 1:
+            from flashattentionanycard_b200.kernels.moe_routing import combine
+
+            self._barrier()
+            combine(self.out, gates_local.reshape(self.tokens_per_rank, self.topk), self.final)
+            return self.final
+        solo = self.world == 1 or self.sync == "none"
+        flags = self._own_flag_ptrs if solo else self.flag_ptrs
+        _native.check(_native.load().bokt_ep_barrier_combine(
+            flags.data_ptr(), self.epoch.data_ptr(), 1 if solo else self.world,
+            0 if solo else self.rank, self.barrier_timeout_ns, self.out.data_ptr(), g.data_ptr(),
+            self.final.data_ptr(), self.tokens_per_rank, self.topk, self.n, self.dtype, stream),
+            "bokt_ep_barrier_combine")
+        return self.final
+
+    def forward(self, x_local, ids_local, gates_local=None, check=False):
         """x_local [tokens_per_rank, K], ids_local [tokens_per_rank, topk] int32 ->
-        [tokens_per_rank * topk, N] (this rank's output buffer, overwritten by
-        the next step): row t*topk + k = x[t] @ W[ids[t, k]].
+
+        * without gates: [tokens_per_rank * topk, N] (this rank's output
+          buffer, overwritten by the next step), row t*topk + k = x[t] @ W[ids[t, k]];
+        * with gates_local [tokens_per_rank, topk] fp32: the MoE layer output in
+          token order, [tokens_per_rank, N], row t = sum_k gates[t, k] x[t] @
+          W[ids[t, k]] (the combine fused into the step's last barrier).
 
         ``check=True`` synchronises after the step and raises RuntimeError if a
         kernel recorded a failure (ids out of range, a packed buffer too small
@@ -581,7 +616,11 @@ class PeerExpertParallelMoE:
         self.dispatch(x_local)
         self._barrier()
         self.compute_and_combine()
-        self._barrier()
+        if gates_local is None:
+            self._barrier()
+            result = self.out
+        else:
+            result = self.barrier_combine(gates_local)
         if check:
             check_device_status(f"expert-parallel step on rank {self.rank}")
-        return self.out
+        return result

@@ -375,6 +375,22 @@ int bokt_ep_barrier(int32_t* const* flag_ptrs, int32_t* epoch, int world, int me
                     int64_t timeout_ns, void* stream);
 
 /*
+ * The step's last barrier with the gate-weighted combine fused into it (the
+ * receive side of the scatter combine): the barrier of bokt_ep_barrier, after
+ * which -- every peer's grouped GEMM having stored its result rows into this
+ * rank's slot buffer y [tokens * k, N], row t * k + j for token t's j-th
+ * expert -- the same kernel writes out[t] = sum_j gates[t k + j] * y[t k + j]
+ * for this rank's `tokens` tokens (fp32, slot order; bit-identical to
+ * bokt_moe_combine with rows = NULL).  epoch: int32[2] (barrier epoch, CTA
+ * count), zero-initialised, shared with bokt_ep_barrier.  A timeout skips the
+ * combine and is recorded as in bokt_ep_barrier.  The combine of the MoE layer
+ * (the reference leaves it outside its operator, kernels/moe_grouped_gemm.py:3).
+ */
+int bokt_ep_barrier_combine(int32_t* const* flag_ptrs, int32_t* epoch, int world, int me,
+                            int64_t timeout_ns, const void* y, const float* gates, void* out,
+                            int tokens, int k, int N, int dtype, void* stream);
+
+/*
  * CUDA IPC plumbing for the expert-parallel peer buffers.  bokt_ipc_export
  * writes the 64-byte IPC handle of the allocation containing `ptr` and the
  * offset of `ptr` inside it (works for sub-allocations of a caching

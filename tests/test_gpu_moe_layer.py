@@ -84,3 +84,57 @@ def test_moe_layer_end_to_end(cuda_device):
                                                                       want_ids])
     ref = np.einsum("tk,tkn->tn", want_gates, per)
     gate(out, ref, "bf16")
+
+
+@pytest.mark.parametrize("world", [1, 2, 4])
+def test_moe_layer_expert_parallel_fused_combine(world, cuda_device):
+    """The MoE layer through the expert-parallel peer path with the combine
+    fused into the step's last barrier (bokt_ep_barrier_combine): logits ->
+    gate -> per-rank dispatch -> grouped GEMM with peer-store scatter ->
+    fused combine.  Ranks share this GPU (phases in stream order).  Each rank's
+    token-order output is bit-identical to the separate combine kernel run on
+    the same slot rows, and passes the gate against the oracle layer."""
+    from flashattentionanycard_b200 import expert_parallel as ep
+    from flashattentionanycard_b200.configs.search_spaces import default_params
+
+    tokens, experts, k_top, hidden, n = 4096, 16, 2, 512, 1024
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(tokens, hidden, generator=g).bfloat16()
+    logits = torch.randn(tokens, experts, generator=g)
+    w = (0.05 * torch.randn(experts, hidden, n, generator=g)).bfloat16()
+    dev = cuda_device
+    ids = torch.empty(tokens, k_top, dtype=torch.int32, device=dev)
+    gates = torch.empty(tokens, k_top, dtype=torch.float32, device=dev)
+    topk_gate(logits.to(dev), k_top, ids, gates)
+    flat = ids.reshape(-1).cpu().numpy()
+    placement = ep.plan_placement(np.bincount(flat, minlength=experts), world)
+    tpr = tokens // world
+    plan = ep.plan_splits(flat, placement, k_top, tpr)
+    wd, xd = w.to(dev), x.to(dev)
+    params = default_params("moe_grouped_gemm")
+    ranks = [ep.PeerExpertParallelMoE(wd[ep.local_weight_slices(placement, r)].contiguous(),
+                                      placement, plan, r, world, k_top, tpr, params=params,
+                                      exchange=False) for r in range(world)]
+    for m in ranks:
+        m.set_peer_pointers([q.x_packed.data_ptr() for q in ranks],
+                            [q.out.data_ptr() for q in ranks])
+        m.ids_global.copy_(ids.reshape(-1))
+        m.final.fill_(float("nan"))
+        m.layout()
+    for r, m in enumerate(ranks):
+        m.dispatch(xd[r * tpr:(r + 1) * tpr])
+    for m in ranks:
+        m.compute_and_combine()
+    finals = [m.barrier_combine(gates[r * tpr:(r + 1) * tpr]).clone()
+              for r, m in enumerate(ranks)]
+    torch.cuda.synchronize()
+    want_ids, want_gates = routing.topk_gate(logits.numpy(), k_top)
+    xf, wf = as_f32(x), as_f32(w)
+    per = np.stack([xf @ wf[e] for e in range(experts)], 1)[np.arange(tokens)[:, None], want_ids]
+    ref = np.einsum("tk,tkn->tn", want_gates, per)
+    for r, m in enumerate(ranks):
+        separate = torch.empty(tpr, n, dtype=torch.bfloat16, device=dev)
+        combine(m.out, gates[r * tpr:(r + 1) * tpr], separate)
+        torch.cuda.synchronize()
+        assert torch.equal(finals[r], separate), "fused combine differs from the combine kernel"
+        gate(finals[r], ref[r * tpr:(r + 1) * tpr], "bf16")
