@@ -59,6 +59,7 @@ L2_BYTES = 126 * 1024 * 1024
 EP_COMM = "peer"  # --ep-comm: expert-parallel dispatch/combine over NVLink peer stores or NCCL
 MOE_EXPERTS = None  # --experts: moe_large with fewer experts (small profiling case)
 PARAM_OVERRIDES = {}  # --params: launch-parameter overrides for the timed workloads
+GEMM_SHAPE = (8192, 8192, 8192)  # --shape of the "gemm" workload
 # Rotating input sets together span 4x L2, so a set is long evicted when it is reused.
 ROTATION_BYTES = 4 * L2_BYTES
 SECONDARY_AUTO = ("gemm8192", "moe_large")
@@ -390,6 +391,12 @@ def rmsnorm_gemm_config(world):
             "params": params_for("gemm")}
 
 
+def gemm_shape_config(world):
+    m, n, k = GEMM_SHAPE
+    return {"workload": f"gemm_bf16_{m}x{n}x{k}", "m": m, "n": n, "k": k, "partition": "replicas",
+            "l2": "rotating A/C sets beyond L2", "params": params_for("gemm")}
+
+
 CONFIGS = {
     "rmsnorm": rmsnorm_config,
     "gemm8192": lambda w: gemm_config(8192, "bf16", True, w),
@@ -399,8 +406,9 @@ CONFIGS = {
     "moe_small": moe_small_config,
     "moe_large": moe_large_config,
     "rmsnorm_gemm": rmsnorm_gemm_config,
+    "gemm": lambda w: gemm_shape_config(w),
 }
-SCALING = {"rmsnorm": "weak", "gemm2048": "weak", "gemm2048_fp16": "weak", "moe_small": "weak",
+SCALING = {"gemm": "weak", "rmsnorm": "weak", "gemm2048": "weak", "gemm2048_fp16": "weak", "moe_small": "weak",
            "gemm8192": "strong", "gemm8192_fp16": "strong", "moe_large": "strong",
            "rmsnorm_gemm": "strong"}
 
@@ -505,6 +513,12 @@ class Gemm:
         s = i % self.sets
         gemm.launch(self.A[s], self.b, self.C[s], self.params)
 
+    def torch_step(self, i):
+        import torch
+
+        s = i % self.sets
+        torch.mm(self.A[s], self.b, out=self.C[s])
+
     def value(self, seconds_per_step, world):
         return self.flops_per_step * world / seconds_per_step / 1e12
 
@@ -533,6 +547,56 @@ class Gemm:
 
         a, bb = self.d_in[b]
         gemm.launch(a, bb, self.d_out[b], self.params)
+
+
+class GemmShape(Gemm):
+    """C = A.B bf16 of any --shape MxNxK (replicas): e.g. the tall-K shapes
+    where split-K pays.  A, B ~ N(0, 1) K^-0.5 as the square configurations."""
+
+    def __init__(self, device, rank, world):
+        import torch
+
+        from flashattentionanycard_b200 import workloads
+
+        m, n, k = GEMM_SHAPE
+        self.name, self.dtype, self.split = "gemm", "bf16", False
+        self.m, self.n_local, self.k = m, n, k
+        self.params = params_for("gemm")
+        self.kernel = (f"gemm_tc2_kernel<{self.params['BLOCK_N']}>"
+                       if self.params.get("CTA_GROUP") == 2
+                       else f"gemm_tc_kernel<{self.params['BLOCK_N']},dense>")
+        a, b = workloads.gemm_inputs(m, n, k, "bf16", seed=0, device=device)
+        self.a, self.b = a, b
+        self.flops_per_step = 2.0 * m * n * k
+        per_set = (m * k + k * n + m * n) * 2
+        self.sets = max(1, math.ceil(ROTATION_BYTES / per_set)) if per_set < ROTATION_BYTES else 1
+        self.A = [a] + [a.roll(i, 0).contiguous() for i in range(1, self.sets)]
+        self.C = [torch.empty(m, n, device=device, dtype=a.dtype) for _ in range(self.sets)]
+        self.size = k
+
+    def parity(self):
+        s = 1 % self.sets
+        rows = sample_rows(self.m, 16)
+        out = gate_check(self.C[s][rows], self.A[s][rows].float() @ self.b.float(), "bf16")
+        out["checked"] = f"{len(rows)} sampled rows x {self.n_local} columns"
+        return out
+
+    def e2e_setup(self):
+        import torch
+
+        self.h_in = [self.a.cpu().pin_memory(), self.b.cpu().pin_memory()]
+        self.d_in = [[torch.empty_like(self.a), torch.empty_like(self.b)] for _ in range(2)]
+        self.d_out = [torch.empty_like(self.C[0]) for _ in range(2)]
+        self.h_out = [torch.empty(self.C[0].shape, dtype=self.a.dtype).pin_memory()
+                      for _ in range(2)]
+        self.h2d = sum(t.numel() * t.element_size() for t in self.h_in)
+        self.d2h = self.h_out[0].numel() * 2
+
+    def torch_step(self, i):
+        import torch
+
+        s = i % self.sets
+        torch.mm(self.A[s], self.b, out=self.C[s])
 
 
 class RmsnormGemm:
@@ -969,8 +1033,9 @@ WORKLOADS = {
     "moe_small": lambda d, r, w: MoeSmall(d, r, w),
     "moe_large": lambda d, r, w: MoeLarge(d, r, w),
     "rmsnorm_gemm": lambda d, r, w: RmsnormGemm(d, r, w),
+    "gemm": lambda d, r, w: GemmShape(d, r, w),
 }
-DEFAULT_STEPS = {"rmsnorm": 4000, "gemm8192": 200, "gemm2048": 2000, "gemm8192_fp16": 200,
+DEFAULT_STEPS = {"gemm": 200, "rmsnorm": 4000, "gemm8192": 200, "gemm2048": 2000, "gemm8192_fp16": 200,
                  "gemm2048_fp16": 2000, "moe_small": 4000,
                  "moe_large": 100, "rmsnorm_gemm": 400}
 
@@ -992,6 +1057,13 @@ class CpuLeg:
             self.cx, self.cw, self.eps = x.float().numpy(), w.float().numpy(), eps
             self.sample = "numpy fp32 RMSNorm of the full 4096x4096 input, rows split over host threads"
             self.work = 2 * m * n * 2 + n * 2
+        elif name == "gemm":
+            m, n, k = GEMM_SHAPE
+            rows = min(m, 256)
+            a, b = workloads.gemm_inputs(rows, n, k, "bf16", seed=0)
+            self.ca, self.cb = a.float().numpy(), b.float().numpy()
+            self.sample = f"numpy/BLAS fp32 GEMM of {rows} rows of A x B (K={k}, N={n})"
+            self.work = 2.0 * rows * n * k
         elif name.startswith("gemm"):
             size = 8192 if name.startswith("gemm8192") else 2048
             dtype = "fp16" if name.endswith("_fp16") else "bf16"
@@ -1303,6 +1375,13 @@ def measure_workload(name, args, steps, ctx):
                            "(normalised x written to and read back from HBM)",
                    "timing": "paired: graphs of 20 fused / 20 unfused steps replayed "
                              "alternately 9 times each, medians"}
+    torch_mm = None
+    if args.compare_torch and hasattr(workload, "torch_step"):
+        ours_ms, torch_ms = paired_graph_times(stream, workload.step, workload.torch_step)
+        torch_mm = {"ms_per_step": torch_ms, "value": workload.value(torch_ms / 1e3, world),
+                    "ours_ms_per_step": ours_ms, "speedup_vs_torch": torch_ms / ours_ms,
+                    "timing": "paired: graphs of 20 launches of ours / torch.mm replayed "
+                              "alternately 9 times each, medians"}
     traffic, traffic_source = profile_traffic(workload.name)
     roofline = {"kernel": workload.kernel, "bound": "hbm" if unit_r == "GB/s" else "tensor",
                 "achieved": achieved, "peak": peak, "unit": unit_r, "frac": achieved / peak,
@@ -1362,6 +1441,8 @@ def measure_workload(name, args, steps, ctx):
     }
     if unfused is not None:
         result["unfused"] = unfused
+    if torch_mm is not None:
+        result["torch_mm"] = torch_mm
     # Free this workload before the next one (peer mappings first, on every rank).
     torch.cuda.synchronize()
     if world > 1:
@@ -1431,8 +1512,9 @@ def run_ours(args):
         "cpu_baseline": head.get("cpu_baseline"), "e2e": head["e2e"], "clocks": head["clocks"],
         "gpu_launches": head["gpu_launches"], "parity": head["parity"], "impl": "ours",
     }
-    if "unfused" in head:
-        line["unfused"] = head["unfused"]
+    for key in ("unfused", "torch_mm"):
+        if key in head:
+            line[key] = head[key]
     if len(results) > 1:
         line["secondary"] = results[1:]
     print(json.dumps(line))
@@ -1473,10 +1555,17 @@ def main():
                          "same kernel, e.g. for ncu captures)")
     ap.add_argument("--ep-comm", choices=("peer", "nccl"), default="peer",
                     help="moe_large at N>1: NVLink peer stores (fused) or NCCL all-to-all")
+    ap.add_argument("--shape", default="8192x8192x8192",
+                    help="MxNxK of the 'gemm' workload (bf16, replicas)")
+    ap.add_argument("--compare-torch", action="store_true",
+                    help="GEMM workloads: also time torch.mm (cuBLAS) paired with ours")
     ap.add_argument("--params", default="",
                     help="launch-parameter overrides, e.g. 'gemm:GROUP_M=16;rmsnorm:num_warps=8'")
     args = ap.parse_args()
-    global EP_COMM, MOE_EXPERTS, PARAM_OVERRIDES
+    global EP_COMM, MOE_EXPERTS, PARAM_OVERRIDES, GEMM_SHAPE
+    GEMM_SHAPE = tuple(int(v) for v in args.shape.lower().split("x"))
+    if len(GEMM_SHAPE) != 3 or min(GEMM_SHAPE) <= 0:
+        raise SystemExit("--shape must be MxNxK")
     EP_COMM = args.ep_comm
     MOE_EXPERTS = args.experts
     PARAM_OVERRIDES = parse_params(args.params)

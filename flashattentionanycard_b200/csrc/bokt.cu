@@ -1314,24 +1314,50 @@ constexpr int64_t kRouteScratchWords = 64 * 1024;  // 256 KiB
 
 static __device__ __align__(256) int32_t g_route_scratch[kRouteScratchWords];
 
-int32_t* g_route_scratch_ptr[kMaxDevices] = {};
+// Resolved device address per device, with the context it was resolved in: a
+// different current context (after cudaDeviceReset, or a user-created
+// context) loads its own copy of the module, so the address is looked up
+// again rather than reusing one from a context that may be gone.
+struct ScratchAddr {
+  CUcontext ctx;
+  int32_t* ptr;
+};
+ScratchAddr g_route_scratch_addr[kMaxDevices] = {};
 std::mutex g_route_scratch_mu;
+PFN_cuCtxGetCurrent_v4000 g_ctx_current = nullptr;
+std::once_flag g_ctx_current_once;
 
-// Device address of g_route_scratch on the current device, resolved on the
-// first call per device (that first call must not be inside stream capture).
+// Device address of g_route_scratch in the current device's current context,
+// resolved on the first call in that context (that first call must not be
+// inside stream capture).
 int route_scratch(int32_t** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (dev < 0 || dev >= kMaxDevices) return fail(BOKT_ERR_UNSUPPORTED, "device index %d", dev);
+  std::call_once(g_ctx_current_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_ctx_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(fn);
+  });
+  if (!g_ctx_current) return fail(BOKT_ERR_CUDA, "cuCtxGetCurrent entry point unavailable");
+  CUcontext ctx = nullptr;
+  if (g_ctx_current(&ctx) != CUDA_SUCCESS) return fail(BOKT_ERR_CUDA, "cuCtxGetCurrent failed");
   std::lock_guard<std::mutex> lock(g_route_scratch_mu);
-  if (!g_route_scratch_ptr[dev]) {
+  ScratchAddr& slot = g_route_scratch_addr[dev];
+  if (!ctx || !slot.ptr || slot.ctx != ctx) {
+    // Also makes the device's primary context current when none is yet.
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_route_scratch);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_route_scratch)");
-    g_route_scratch_ptr[dev] = static_cast<int32_t*>(p);
+    if (g_ctx_current(&ctx) != CUDA_SUCCESS || !ctx)
+      return fail(BOKT_ERR_CUDA, "no current CUDA context");
+    slot.ctx = ctx;
+    slot.ptr = static_cast<int32_t*>(p);
   }
-  *out = g_route_scratch_ptr[dev];
+  *out = slot.ptr;
   return BOKT_OK;
 }
 

@@ -241,8 +241,10 @@ int bokt_moe_route(const int32_t* expert_ids, int A, int E, int32_t* counts, int
  * ceil(A / 4096) * E <= bokt_moe_route_noalloc_max_words() (65536), e.g.
  * 32768 assignments x 1024 experts or 1,048,576 x 256; larger requests fail
  * with BOKT_ERR_UNSUPPORTED and a message, nothing is launched.  The first call
- * on each device looks the array's device address up (cudaGetSymbolAddress),
- * so make that first call outside stream capture.  All calls on a device share
+ * on each device, and again in any new CUDA context on it (after a device
+ * reset, or with a context of the caller's own), looks the array's device
+ * address up (cudaGetSymbolAddress), so make that first call outside stream
+ * capture.  All calls on a device share
  * the one array: calls that overlap on the GPU (different streams, no ordering
  * between them) race and give wrong results; calls in one stream are fine.
  * Outputs are identical to bokt_moe_route's.  Allocates nothing.

@@ -3,7 +3,7 @@
 Runs only where the reference checkout is present (the build container); the
 committed ``*.npz`` files are what the tests read.  Usage:
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py PATH_TO_REFERENCE_CHECKOUT
 
 For every case it records:
   * the inputs (16-bit storage bits), drawn exactly as the reference's
@@ -116,4 +116,6 @@ def main(reference_root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py PATH_TO_REFERENCE_CHECKOUT")
+    main(sys.argv[1])
