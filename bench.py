@@ -193,6 +193,10 @@ def paired_graph_times(stream, fn_a, fn_b, count=20, reps=9):
     import torch
 
     graphs = []
+    with torch.cuda.stream(stream):
+        for fn in (fn_a, fn_b):  # library set-up (cuBLAS handles, workspaces) before capture
+            fn(0)
+    torch.cuda.synchronize()
     for fn in (fn_a, fn_b):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):

@@ -152,6 +152,19 @@ struct TileCoord {
   int rows_valid;  // rows of this tile inside the problem (<= 128)
 };
 
+// K-loop direction of a worker's i-th tile (dense GEMM, whole tiles): odd
+// tiles of a persistent worker run their k-blocks last to first.  The
+// workers' i-th tiles form wave i of the raster, and consecutive waves share
+// operand rows (the same A rows in the GROUP_M order), so a wave that starts
+// where the previous one ended finds those k-blocks still in L2.  The MMA
+// issuer consumes stages in ring order either way; only the fp32 summation
+// order of the tile changes.  Grouped GEMMs keep one order so that a row's
+// result does not depend on the grid.
+template <bool GROUPED>
+__device__ __forceinline__ bool k_reversed_for(int i, int split) {
+  return !GROUPED && split <= 1 && (i & 1);
+}
+
 __device__ __forceinline__ TileCoord dense_tile(int t, int M, int nn, int group_m, int bn) {
   // GROUP_M rasterisation, same mapping as kernels/gemm.py:20-26.
   const int nm = (M + kGemmBM - 1) / kGemmBM;
@@ -435,9 +448,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool ok = true;
       SegmentCursor cur = segment_cursor(worker, workers, ntiles, split);
       Segment sg;
-      while (ok && segment_next(cur, split, nkb, sg)) {
+      for (int i = 0; ok && segment_next(cur, split, nkb, sg); ++i) {
         const TileCoord tc = tile_at(sg.tile);
-        for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
+        const bool rev = k_reversed_for<GROUPED>(i, split);
+        for (int kk = sg.kb0; kk < sg.kb1; ++kk) {
+          const int kb = rev ? sg.kb1 - 1 - (kk - sg.kb0) : kk;
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, 1)) {
             ok = false;
             break;

@@ -158,9 +158,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool ok = true;
       SegmentCursor cur = segment_cursor(pair, workers, ntiles, split);
       Segment sg;
-      while (ok && segment_next(cur, split, nkb, sg)) {
+      for (int i = 0; ok && segment_next(cur, split, nkb, sg); ++i) {
         const TileCoord tc = tile_at(sg.tile);
-        for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
+        const bool rev = k_reversed_for<GROUPED>(i, split);
+        for (int kk = sg.kb0; kk < sg.kb1; ++kk) {
+          const int kb = rev ? sg.kb1 - 1 - (kk - sg.kb0) : kk;
           if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, abort_flag, 11)) {
             ok = false;
             break;
