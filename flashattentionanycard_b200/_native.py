@@ -217,7 +217,7 @@ class CompiledKernel:
         self.n_regs = int(attrs.registers)
         self.n_spills = int(attrs.local_bytes) // 4
         self.threads = int(attrs.threads)
-        self.path = {0: "tcgen05", 1: "simt", 2: "vector", 3: "scalar", 4: "ring",
+        self.path = {0: "tcgen05", 1: "tcgen05_edge", 2: "vector", 3: "scalar", 4: "ring",
                      5: "pipelined"}.get(attrs.path, "?")
 
 

@@ -13,7 +13,7 @@
 #include "../../include/bokt.h"
 #include "bokt_device.cuh"
 #include "ep_sync.cuh"
-#include "gemm_simt.cuh"
+#include "gemm_edge.cuh"
 #include "gemm_tc.cuh"
 #include "gemm_tc2.cuh"
 #include "moe_route.cuh"
@@ -347,14 +347,21 @@ int launch_tc(bool grouped, int dtype, const TcConfig& cfg, const CUtensorMap& m
   return BOKT_OK;
 }
 
+// Edge shapes (row strides TMA cannot describe): the tcgen05 edge kernel, one
+// CTA per 128 x 64 tile.  Dense: experts == 0, rows = M; grouped: rows = T.
 template <typename T>
-int launch_simt(const void* A, const void* B, void* C, int rows, int N, int K,
-                const void* offsets, int offsets_i64, int experts, cudaStream_t s) {
-  dim3 grid((N + bokt::kSimtCols - 1) / bokt::kSimtCols, rows < 65535 ? rows : 65535);
-  cudaError_t e = launch(bokt::gemm_simt_kernel<T>, grid, dim3(bokt::kSimtCols), 0, s,
+int launch_edge(const void* A, const void* B, void* C, int rows, int N, int K,
+                const void* offsets, int offsets_i64, int experts, int dtype, cudaStream_t s) {
+  const long long nn = (N + bokt::kEdgeBN - 1) / bokt::kEdgeBN;
+  const long long mtiles = (rows + bokt::kEdgeBM - 1) / bokt::kEdgeBM + (experts > 0 ? experts : 0);
+  const long long tiles = mtiles * nn;
+  if (tiles > 0x7fffffffLL) return fail(BOKT_ERR_UNSUPPORTED, "edge path: too many tiles");
+  const uint32_t idesc = bokt::make_idesc_f16(uint32_t(dtype), bokt::kEdgeBM, bokt::kEdgeBN);
+  cudaError_t e = launch(bokt::gemm_tc_edge_kernel<T>, dim3(unsigned(tiles)),
+                         dim3(bokt::kEdgeThreads), bokt::kEdgeSmemBytes, s,
                          static_cast<const T*>(A), static_cast<const T*>(B), static_cast<T*>(C),
-                         rows, N, K, offsets, offsets_i64, experts);
-  if (e != cudaSuccess) return cuda_fail(e, "gemm_simt launch");
+                         rows, N, K, offsets, offsets_i64, experts, idesc);
+  if (e != cudaSuccess) return cuda_fail(e, "gemm_tc_edge launch");
   return BOKT_OK;
 }
 
@@ -380,8 +387,9 @@ int dense_gemm_impl(const void* A, const void* B, void* C, int M, int N, int K, 
       return fail(BOKT_ERR_UNSUPPORTED,
                   "fused RMSNorm-GEMM needs K > 0, K and N multiples of 8 and 16-byte aligned "
                   "operands (got M=%d N=%d K=%d)", M, N, K);
-    return dtype == BOKT_BF16 ? launch_simt<__nv_bfloat16>(A, B, C, M, N, K, nullptr, 0, 0, s)
-                              : launch_simt<__half>(A, B, C, M, N, K, nullptr, 0, 0, s);
+    return dtype == BOKT_BF16
+               ? launch_edge<__nv_bfloat16>(A, B, C, M, N, K, nullptr, 0, 0, dtype, s)
+               : launch_edge<__half>(A, B, C, M, N, K, nullptr, 0, 0, dtype, s);
   }
   TcConfig cfg;
   rc = resolve_tc_config(params, false, 0, dev.smem_optin, &cfg);
@@ -454,7 +462,7 @@ int resolve_norm_config(const bokt_params* p, int N, bool vec_ok, NormConfig* ou
   if (stages < 1 || stages > 32) return fail(BOKT_ERR_CONFIG, "stages must be in [1, 32]");
   // The ring kernel streams whole rows with cp.async.bulk (16-byte multiples,
   // 16-byte aligned); odd or unaligned rows take the per-row kernels instead,
-  // as odd GEMM shapes take the SIMT edge path.
+  // as odd GEMM shapes take the edge GEMM kernel.
   int ring = 0;
   if (stages == 2 && vec_ok && rows == 1 && vpt > 0 && vpt <= 8) {
     // Two register buffers: the persistent software-pipelined kernel (one row
@@ -661,8 +669,8 @@ int grouped_gemm_impl(const void* X, const void* W, const void* offsets, int off
       return fail(BOKT_ERR_UNSUPPORTED,
                   "scatter epilogue needs the tcgen05 path (K, N multiples of 8, aligned)");
     return dtype == BOKT_BF16
-               ? launch_simt<__nv_bfloat16>(X, W, Y, T, N, K, offsets, offsets_is_i64, E, s)
-               : launch_simt<__half>(X, W, Y, T, N, K, offsets, offsets_is_i64, E, s);
+               ? launch_edge<__nv_bfloat16>(X, W, Y, T, N, K, offsets, offsets_is_i64, E, dtype, s)
+               : launch_edge<__half>(X, W, Y, T, N, K, offsets, offsets_is_i64, E, dtype, s);
   }
   const bokt_params zero = {};
   TcConfig cfg;
@@ -1210,9 +1218,11 @@ int bokt_kernel_attrs(int kernel, int dtype, int n, int k, const bokt_params* pa
     } else if (norm) {
       return fail(BOKT_ERR_UNSUPPORTED, "fused RMSNorm-GEMM needs K and N multiples of 8");
     } else {
-      fn = dtype == BOKT_BF16 ? reinterpret_cast<const void*>(&bokt::gemm_simt_kernel<__nv_bfloat16>)
-                              : reinterpret_cast<const void*>(&bokt::gemm_simt_kernel<__half>);
-      threads = bokt::kSimtCols;
+      fn = dtype == BOKT_BF16
+               ? reinterpret_cast<const void*>(&bokt::gemm_tc_edge_kernel<__nv_bfloat16>)
+               : reinterpret_cast<const void*>(&bokt::gemm_tc_edge_kernel<__half>);
+      threads = bokt::kEdgeThreads;
+      dyn = bokt::kEdgeSmemBytes;
       path = 1;
     }
   } else if (kernel == BOKT_KERNEL_RMSNORM) {

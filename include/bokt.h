@@ -100,7 +100,7 @@ typedef struct bokt_attrs {
   int32_t local_bytes;    /* local memory per thread (spill indicator) */
   int32_t threads;        /* threads per CTA */
   int32_t max_threads;    /* cudaFuncAttributes.maxThreadsPerBlock */
-  int32_t path; /* 0 tcgen05/TMA, 1 SIMT edge, 2 vector, 3 scalar, 4 ring, 5 pipelined */
+  int32_t path; /* 0 tcgen05/TMA, 1 tcgen05 edge, 2 vector, 3 scalar, 4 ring, 5 pipelined */
 } bokt_attrs;
 
 /* ABI version and the sm architecture the library was built for (100). */
@@ -114,8 +114,10 @@ const char* bokt_last_error(void);
  * C[M,N] = A[M,K] * B[K,N]; all row-major, contiguous, same element type;
  * fp32 accumulation, result rounded to the element type on store.  Every
  * element of C is written.  Replaces kernels/gemm.py:43-48.
- * Shapes with K % 8, N % 8 or a pointer not 16-byte aligned take the SIMT edge
- * path (TMA needs 16-byte row strides); everything else runs on tcgen05.
+ * Shapes with K % 8, N % 8 or a pointer not 16-byte aligned (row strides TMA
+ * cannot describe) take the tcgen05 edge kernel: masked element loads into the
+ * swizzled shared-memory tiles, 128 x 64 tiles, still on tensor cores; everything
+ * else runs on the TMA-fed tcgen05 kernels.
  */
 int bokt_gemm(const void* A, const void* B, void* C, int M, int N, int K, int dtype,
               const bokt_params* params, void* stream);
