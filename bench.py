@@ -290,9 +290,17 @@ def rmsnorm_config(world):
             "params": params_for("rmsnorm")}
 
 
+def rotating_sets(per_set_bytes):
+    """Input sets to rotate through so that together they exceed L2 by 4x,
+    at most 64 (tiny problems stay L2-resident anyway; the cap keeps set-up
+    short)."""
+    if per_set_bytes >= ROTATION_BYTES:
+        return 1
+    return min(64, max(1, math.ceil(ROTATION_BYTES / per_set_bytes)))
+
+
 def gemm_sets(size, n_local):
-    per_set = (size * size + 2 * size * n_local) * 2
-    return max(1, math.ceil(ROTATION_BYTES / per_set)) if per_set < ROTATION_BYTES else 1
+    return rotating_sets((size * size + 2 * size * n_local) * 2)
 
 
 def gemm_config(size, dtype, split, world):
@@ -397,8 +405,10 @@ def rmsnorm_gemm_config(world):
 
 def gemm_shape_config(world):
     m, n, k = GEMM_SHAPE
+    sets = rotating_sets((m * k + k * n + m * n) * 2)
     return {"workload": f"gemm_bf16_{m}x{n}x{k}", "m": m, "n": n, "k": k, "partition": "replicas",
-            "l2": "rotating A/C sets beyond L2", "params": params_for("gemm")}
+            "l2": "inputs > L2" if sets == 1 else f"rotating {sets} A/C sets",
+            "params": params_for("gemm")}
 
 
 CONFIGS = {
@@ -573,7 +583,7 @@ class GemmShape(Gemm):
         self.a, self.b = a, b
         self.flops_per_step = 2.0 * m * n * k
         per_set = (m * k + k * n + m * n) * 2
-        self.sets = max(1, math.ceil(ROTATION_BYTES / per_set)) if per_set < ROTATION_BYTES else 1
+        self.sets = rotating_sets(per_set)
         self.A = [a] + [a.roll(i, 0).contiguous() for i in range(1, self.sets)]
         self.C = [torch.empty(m, n, device=device, dtype=a.dtype) for _ in range(self.sets)]
         self.size = k

@@ -5,16 +5,18 @@
 // Triton kernel runs them on tensor cores with masked loads
 // (kernels/gemm.py:33-38).
 //
-// One CTA (4 warps) per 128 x 64 output tile, tcgen05.mma.cta_group::1 with
+// One CTA (8 warps) per 128 x 64 output tile, tcgen05.mma.cta_group::1 with
 // M = 128, N = 64 accumulating in 64 TMEM columns.  Per 64-wide k-block the
 // CTA's threads load the A tile (128 rows x 64 k) and the B tile (64 k x 64
 // columns) element by element with bounds checks (zero outside the matrix)
-// straight into the 128-byte-swizzled shared-memory layouts the TMA path
-// produces, so the MMA uses the same descriptors; one elected thread issues
-// the four K = 16 MMAs and commits them to an mbarrier that every thread
-// waits on (bounded) before the tile buffers are refilled.  The epilogue
-// reads TMEM (warp w holds tile rows 32 w .. 32 w + 31) and stores every
-// element inside the matrix, rounded to the element type.
+// into registers, then write them into the 128-byte-swizzled shared-memory
+// layouts the TMA path produces, so the MMA uses the same descriptors; one
+// elected thread issues the four K = 16 MMAs and commits them to an mbarrier
+// that every thread waits on (bounded) before the tile buffers are refilled,
+// while the next k-block's loads are already in flight.  The epilogue
+// reads TMEM (warp w: tile rows 32 (w % 4) .. +31, the lane quadrant it may
+// access, and columns 32 (w / 4) .. +31) and stores every element inside the
+// matrix, rounded to the element type.
 //
 // Same semantics as the main path: fp32 accumulation, every covered element
 // written, rows outside the experts' ranges (grouped) left alone.
@@ -27,7 +29,8 @@ namespace bokt {
 constexpr int kEdgeBM = 128;
 constexpr int kEdgeBN = 64;
 constexpr int kEdgeBK = 64;
-constexpr int kEdgeThreads = 128;
+constexpr int kEdgeThreads = 256;
+constexpr int kEdgeRowStep = kEdgeThreads / 64;  // rows a thread skips between its loads
 constexpr int kEdgeABytes = kEdgeBM * kEdgeBK * 2;  // 16 KB
 constexpr int kEdgeBBytes = kEdgeBK * kEdgeBN * 2;  // 8 KB
 constexpr int kEdgeSmemBytes = 1024 + kEdgeABytes + kEdgeBBytes + 64;
@@ -126,22 +129,40 @@ __global__ void __launch_bounds__(kEdgeThreads) gemm_tc_edge_kernel(
 
   bool ok = a_row >= 0 && valid > 0;  // uniform: CTA past the last grouped tile does nothing
   const int nkb = (K + kEdgeBK - 1) / kEdgeBK;
-  for (int kb = 0; ok && kb < nkb; ++kb) {
+  // Thread t loads column c = t % 64 of the tiles (k for A, n for B) in rows
+  // r0, r0 + 4, ... (r0 = t / 64): a warp reads 32 consecutive elements of a
+  // row.  Each k-block's elements are loaded into registers first (all loads
+  // in flight together), then written to shared memory; the next k-block's
+  // loads are issued while the tensor cores work on the current one.
+  const int c = threadIdx.x & 63;
+  const int r0 = threadIdx.x >> 6;
+  const bool n_ok = n0 + c < N;
+  constexpr int kAPer = kEdgeBM / kEdgeRowStep, kBPer = kEdgeBK / kEdgeRowStep;
+  T va[kAPer], vb[kBPer];
+  const T* a_col = A + static_cast<size_t>(a_row + r0) * K + c;
+  const T* b_col = Bp + static_cast<size_t>(r0) * N + n0 + c;
+  const size_t a_step = static_cast<size_t>(kEdgeRowStep) * K;
+  const size_t b_step = static_cast<size_t>(kEdgeRowStep) * N;
+  auto load_block = [&](int kb) {
     const int k0 = kb * kEdgeBK;
-    // A tile: consecutive threads take consecutive k of one row (coalesced).
-    for (int i = threadIdx.x; i < kEdgeBM * kEdgeBK; i += kEdgeThreads) {
-      const int r = i / kEdgeBK, k = i - r * kEdgeBK;
-      T v = zero;
-      if (r < valid && k0 + k < K) v = A[static_cast<size_t>(a_row + r) * K + k0 + k];
-      *reinterpret_cast<T*>(sA + sw128_offset(r, k)) = v;
-    }
-    // B tile (N-major): consecutive threads take consecutive columns of one k row.
-    for (int i = threadIdx.x; i < kEdgeBK * kEdgeBN; i += kEdgeThreads) {
-      const int kr = i / kEdgeBN, n = i - kr * kEdgeBN;
-      T v = zero;
-      if (k0 + kr < K && n0 + n < N) v = Bp[static_cast<size_t>(k0 + kr) * N + n0 + n];
-      *reinterpret_cast<T*>(sB + sw128_offset(kr, n)) = v;
-    }
+    const bool k_ok = k0 + c < K;
+    const T* pa = a_col + k0;
+#pragma unroll
+    for (int j = 0; j < kAPer; ++j)
+      va[j] = (k_ok && r0 + kEdgeRowStep * j < valid) ? pa[j * a_step] : zero;
+    const T* pb = b_col + static_cast<size_t>(k0) * N;
+#pragma unroll
+    for (int j = 0; j < kBPer; ++j)
+      vb[j] = (n_ok && k0 + r0 + kEdgeRowStep * j < K) ? pb[j * b_step] : zero;
+  };
+  if (ok && nkb > 0) load_block(0);
+  for (int kb = 0; ok && kb < nkb; ++kb) {
+#pragma unroll
+    for (int j = 0; j < kAPer; ++j)
+      *reinterpret_cast<T*>(sA + sw128_offset(r0 + kEdgeRowStep * j, c)) = va[j];
+#pragma unroll
+    for (int j = 0; j < kBPer; ++j)
+      *reinterpret_cast<T*>(sB + sw128_offset(r0 + kEdgeRowStep * j, c)) = vb[j];
     // The tensor cores read shared memory through the async proxy.
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
@@ -157,33 +178,31 @@ __global__ void __launch_bounds__(kEdgeThreads) gemm_tc_edge_kernel(
       }
       umma_commit(bar);
     }
+    if (kb + 1 < nkb) load_block(kb + 1);
     ok = mbar_wait(bar, static_cast<uint32_t>(kb & 1), abort_flag, 31);
     ok = __syncthreads_and(ok);
     tc_fence_after();
   }
+  const int q = warp & 3;         // TMEM lane quadrant: tile rows 32 q .. 32 q + 31
+  const int half = warp >> 2;     // columns 32 half .. 32 half + 31
+  const int r = q * 32 + lane;
+  const int col0 = half * 32;
   if (ok && nkb > 0) {
-    uint32_t v0[32], v1[32];
-    const uint32_t taddr = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
-    tmem_ld_32x32b_x32(taddr, v0);
-    tmem_ld_32x32b_x32(taddr + 32, v1);
+    uint32_t v[32];
+    tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                           static_cast<uint32_t>(col0), v);
     tmem_ld_wait();
-    const int r = warp * 32 + lane;
     if (r < valid) {
-      T* crow = C + static_cast<size_t>(a_row + r) * N + n0;
-      const int ncols = min(kEdgeBN, N - n0);
+      T* crow = C + static_cast<size_t>(a_row + r) * N + n0 + col0;
+      const int ncols = min(32, N - n0 - col0);
 #pragma unroll
-      for (int c = 0; c < 32; ++c)
-        if (c < ncols) crow[c] = Pack2<T>::from_float(__uint_as_float(v0[c]));
-#pragma unroll
-      for (int c = 0; c < 32; ++c)
-        if (32 + c < ncols) crow[32 + c] = Pack2<T>::from_float(__uint_as_float(v1[c]));
+      for (int j = 0; j < 32; ++j)
+        if (j < ncols) crow[j] = Pack2<T>::from_float(__uint_as_float(v[j]));
     }
-  } else if (ok && valid > 0) {
+  } else if (ok && valid > 0 && r < valid) {
     // K == 0: C = 0 for the tile.
-    const int r = warp * 32 + lane;
-    if (r < valid)
-      for (int c = 0; c < kEdgeBN && n0 + c < N; ++c)
-        C[static_cast<size_t>(a_row + r) * N + n0 + c] = zero;
+    for (int j = 0; j < 32 && n0 + col0 + j < N; ++j)
+      C[static_cast<size_t>(a_row + r) * N + n0 + col0 + j] = zero;
   }
   tc_fence_before();
   __syncthreads();

@@ -36,4 +36,8 @@ def launch(a, b, out, params):
                          ctypes.byref(p), ws, ws_bytes, _native.current_stream(a.device)),
         "bokt_gemm",
     )
-    return _native.kernel_attrs(_native.KERNEL_GEMM, dtype, n, k, params, a.device.index)
+    # The library takes the edge kernel for any operand not 16-byte aligned;
+    # report that kernel's attributes then (k = 1 selects it in the query).
+    aligned = all(t.data_ptr() % 16 == 0 for t in (a, b, out))
+    return _native.kernel_attrs(_native.KERNEL_GEMM, dtype, n, k if aligned else 1, params,
+                                a.device.index)

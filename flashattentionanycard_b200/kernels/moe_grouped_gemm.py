@@ -53,5 +53,8 @@ def launch(x, weights, offsets, out, params, sm_count):
         ),
         "bokt_moe_grouped_gemm",
     )
-    return _native.kernel_attrs(_native.KERNEL_MOE_GROUPED_GEMM, dtype, n, k, params,
-                                x.device.index)
+    # The library takes the edge kernel for any operand not 16-byte aligned;
+    # report that kernel's attributes then (k = 1 selects it in the query).
+    aligned = all(t.data_ptr() % 16 == 0 for t in (x, weights, out))
+    return _native.kernel_attrs(_native.KERNEL_MOE_GROUPED_GEMM, dtype, n, k if aligned else 1,
+                                params, x.device.index)
