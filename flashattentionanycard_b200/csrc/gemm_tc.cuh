@@ -152,17 +152,20 @@ struct TileCoord {
   int rows_valid;  // rows of this tile inside the problem (<= 128)
 };
 
-// K-loop direction of a worker's i-th tile (dense GEMM, whole tiles): odd
-// tiles of a persistent worker run their k-blocks last to first.  The
-// workers' i-th tiles form wave i of the raster, and consecutive waves share
-// operand rows (the same A rows in the GROUP_M order), so a wave that starts
-// where the previous one ended finds those k-blocks still in L2.  The MMA
-// issuer consumes stages in ring order either way; only the fp32 summation
-// order of the tile changes.  Grouped GEMMs keep one order so that a row's
-// result does not depend on the grid.
+// K-loop direction of a tile.  Consecutive waves of the persistent raster
+// share operand rows (dense: the same A rows in the GROUP_M order; grouped:
+// an expert's X rows, re-read for each of its weight column blocks), so a
+// tile that starts on the k-blocks another tile has just finished finds them
+// still in L2.  Dense: a worker's odd tiles (odd waves) run their k-blocks
+// last to first.  Grouped: tiles of odd weight column blocks run last to
+// first, a property of the tile itself, so a row's result does not depend on
+// the grid (expert-parallel paths with different grids stay bit-identical).
+// The MMA issuer consumes stages in ring order either way; only the fp32
+// summation order of the tile changes.  Split-K segments keep one order.
 template <bool GROUPED>
-__device__ __forceinline__ bool k_reversed_for(int i, int split) {
-  return !GROUPED && split <= 1 && (i & 1);
+__device__ __forceinline__ bool k_reversed_for(int i, int split, int n0, int bn) {
+  if (split > 1) return false;
+  return GROUPED ? ((n0 / bn) & 1) != 0 : (i & 1) != 0;
 }
 
 __device__ __forceinline__ TileCoord dense_tile(int t, int M, int nn, int group_m, int bn) {
@@ -450,7 +453,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       Segment sg;
       for (int i = 0; ok && segment_next(cur, split, nkb, sg); ++i) {
         const TileCoord tc = tile_at(sg.tile);
-        const bool rev = k_reversed_for<GROUPED>(i, split);
+        const bool rev = k_reversed_for<GROUPED>(i, split, tc.n0, BN);
         for (int kk = sg.kb0; kk < sg.kb1; ++kk) {
           const int kb = rev ? sg.kb1 - 1 - (kk - sg.kb0) : kk;
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, 1)) {

@@ -160,7 +160,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       Segment sg;
       for (int i = 0; ok && segment_next(cur, split, nkb, sg); ++i) {
         const TileCoord tc = tile_at(sg.tile);
-        const bool rev = k_reversed_for<GROUPED>(i, split);
+        const bool rev = k_reversed_for<GROUPED>(i, split, tc.n0, BN);
         for (int kk = sg.kb0; kk < sg.kb1; ++kk) {
           const int kb = rev ? sg.kb1 - 1 - (kk - sg.kb0) : kk;
           if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, abort_flag, 11)) {
