@@ -782,7 +782,11 @@ int bokt_ep_plan(const int32_t* counts, const int32_t* offsets, const int32_t* r
   if (!counts || !offsets || !replicas || !v_rank || !capacity || !v_plo || !v_size ||
       !v_lbase || !loffs || !rank_rows)
     return fail(BOKT_ERR_INVALID, "null pointer");
-  cudaError_t e = launch(bokt::ep_plan_kernel, dim3(1), dim3(32), 0,
+  const int smem = bokt::ep_plan_smem_bytes(E, V, world);
+  if (smem > 200 * 1024) return fail(BOKT_ERR_UNSUPPORTED, "ep_plan: E, V or world too large");
+  int rc = ensure_smem(reinterpret_cast<const void*>(&bokt::ep_plan_kernel), smem);
+  if (rc) return rc;
+  cudaError_t e = launch(bokt::ep_plan_kernel, dim3(1), dim3(256), smem,
                          static_cast<cudaStream_t>(stream), counts, offsets, replicas, E, v_rank,
                          V, world, me, capacity, v_plo, v_size, v_lbase, loffs, rank_rows);
   if (e != cudaSuccess) return cuda_fail(e, "ep_plan launch");

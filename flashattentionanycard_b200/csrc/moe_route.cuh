@@ -276,15 +276,23 @@ namespace bokt {
 
 constexpr int kStatusCapacity = 4;
 
-// Per-step expert-parallel layout from the global routing (one CTA, serial
-// over virtual experts; V is at most a few hundred).  Virtual expert v =
+// Per-step expert-parallel layout from the global routing.  Virtual expert v =
 // (expert e, replica j) serves the contiguous packed rows
 // [v_plo[v], v_plo[v] + v_size[v]) of the global routing; on its rank it is
 // stored at rows [v_lbase[v], v_lbase[v] + v_size[v]) of the packed buffer,
 // virtual experts in ascending v.  loffs = the local grouped-GEMM offsets of
 // rank `me` (n_local + 1 entries).  rank_rows[r] = rows rank r serves; a rank
 // over its buffer capacity is reported (kStatusCapacity).
-__global__ void ep_plan_kernel(const int32_t* __restrict__ counts,
+//
+// One CTA: the inputs are loaded into shared memory by all threads, one
+// thread runs the two short serial passes there (E experts, V virtual
+// experts: a few hundred shared-memory operations), and all threads write
+// the results back.  Dynamic shared memory: ep_plan_smem_bytes(E, V, world).
+__host__ __device__ inline int ep_plan_smem_bytes(int E, int V, int world) {
+  return (3 * E + 5 * V + world + 2) * 4;
+}
+
+__global__ void __launch_bounds__(256, 1) ep_plan_kernel(const int32_t* __restrict__ counts,
                                const int32_t* __restrict__ offsets,
                                const int32_t* __restrict__ replicas, int E,
                                const int32_t* __restrict__ v_rank, int V, int world, int me,
@@ -292,31 +300,66 @@ __global__ void ep_plan_kernel(const int32_t* __restrict__ counts,
                                int32_t* __restrict__ v_plo, int32_t* __restrict__ v_size,
                                int32_t* __restrict__ v_lbase, int32_t* __restrict__ loffs,
                                int32_t* __restrict__ rank_rows) {
+  extern __shared__ int32_t plan_smem[];
+  int32_t* s_cnt = plan_smem;
+  int32_t* s_off = s_cnt + E;
+  int32_t* s_rep = s_off + E;
+  int32_t* s_vrank = s_rep + E;
+  int32_t* s_vsize = s_vrank + V;
+  int32_t* s_vplo = s_vsize + V;
+  int32_t* s_vlbase = s_vplo + V;
+  int32_t* s_loffs = s_vlbase + V;  // V + 1 entries
+  int32_t* s_rrows = s_loffs + V + 1;
+  __shared__ int s_nl;
   pdl_allow_next();
   pdl_wait();
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  int v = 0;
-  for (int e = 0; e < E; ++e) {
-    const long long c = counts[e];
-    const int R = replicas[e];
-    for (int j = 0; j < R; ++j, ++v) {
-      const long long lo = (static_cast<long long>(j) * c + R - 1) / R;  // ceil(j c / R)
-      const long long hi = (static_cast<long long>(j + 1) * c + R - 1) / R;
-      v_plo[v] = offsets[e] + static_cast<int>(lo);
-      v_size[v] = static_cast<int>(hi - lo);
+  for (int i = threadIdx.x; i < E; i += blockDim.x) {
+    s_cnt[i] = counts[i];
+    s_off[i] = offsets[i];
+    s_rep[i] = replicas[i];
+  }
+  for (int i = threadIdx.x; i < V; i += blockDim.x) s_vrank[i] = v_rank[i];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int v = 0;
+    for (int e = 0; e < E; ++e) {
+      const long long c = s_cnt[e];
+      const int R = s_rep[e];
+      for (int j = 0; j < R && v < V; ++j, ++v) {
+        const long long lo = (static_cast<long long>(j) * c + R - 1) / R;  // ceil(j c / R)
+        const long long hi = (static_cast<long long>(j + 1) * c + R - 1) / R;
+        s_vplo[v] = s_off[e] + static_cast<int>(lo);
+        s_vsize[v] = static_cast<int>(hi - lo);
+      }
     }
+    for (; v < V; ++v) s_vplo[v] = s_vsize[v] = 0;  // replicas inconsistent with V
+    for (int r = 0; r < world; ++r) s_rrows[r] = 0;
+    int nl = 0;
+    s_loffs[0] = 0;
+    for (v = 0; v < V; ++v) {
+      const int r = s_vrank[v];
+      if (r < 0 || r >= world) {
+        report_status(kStatusPlanMismatch, v);
+        s_vlbase[v] = 0;
+        continue;
+      }
+      s_vlbase[v] = s_rrows[r];
+      s_rrows[r] += s_vsize[v];
+      if (r == me) s_loffs[++nl] = s_rrows[r];
+    }
+    s_nl = nl;
   }
-  for (int r = 0; r < world; ++r) rank_rows[r] = 0;
-  int nl = 0;
-  loffs[0] = 0;
-  for (v = 0; v < V; ++v) {
-    const int r = v_rank[v];
-    v_lbase[v] = rank_rows[r];
-    rank_rows[r] += v_size[v];
-    if (r == me) loffs[++nl] = rank_rows[r];
+  __syncthreads();
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    v_plo[i] = s_vplo[i];
+    v_size[i] = s_vsize[i];
+    v_lbase[i] = s_vlbase[i];
   }
-  for (int r = 0; r < world; ++r)
-    if (rank_rows[r] > capacity[r]) report_status(kStatusCapacity, r);
+  for (int i = threadIdx.x; i <= s_nl; i += blockDim.x) loffs[i] = s_loffs[i];
+  for (int r = threadIdx.x; r < world; r += blockDim.x) {
+    rank_rows[r] = s_rrows[r];
+    if (s_rrows[r] > capacity[r]) report_status(kStatusCapacity, r);
+  }
 }
 
 __device__ __forceinline__ int ep_virtual_expert(int p, int e, const int32_t* offsets,
