@@ -91,6 +91,7 @@ SIGNATURES = {
     "bokt_gemm_ex": (_I32, [_VP, _VP, _VP, _I32, _I32, _I32, _I32, _PP, _VP, _I64, _VP]),
     "bokt_gemm_workspace_bytes": (_I64, [_I32, _PP]),
     "bokt_splitk_schedule": (_I32, [_I32, _I32, _I32, _I32, _VP, _I32]),
+    "bokt_splitk_reduce_sources": (_I32, [_I32, _I32, _I32, _I32, _VP, _I32]),
     "bokt_moe_grouped_gemm_ex": (
         _I32,
         [_VP, _VP, _VP, _I32, _VP, _I32, _I32, _I32, _I32, _I32, _I32, _PP, _VP, _I64, _VP],
@@ -264,6 +265,18 @@ def splitk_schedule(ntiles, split_k, nkb, launched):
     buf = (ctypes.c_int32 * (6 * max(n, 1)))()
     lib.bokt_splitk_schedule(ntiles, split_k, nkb, launched, buf, n)
     return [tuple(buf[6 * i:6 * i + 6]) for i in range(n)]
+
+
+def splitk_reduce_sources(ntiles, split_k, nkb, launched):
+    """Partials the separate split-K reduction adds, in its order: list of
+    (tile, worker, which) -- workspace slot 2 c + which of worker CTA slot c."""
+    lib = load()
+    n = lib.bokt_splitk_reduce_sources(ntiles, split_k, nkb, launched, None, 0)
+    if n < 0:
+        raise RuntimeError(lib.bokt_last_error().decode())
+    buf = (ctypes.c_int32 * (3 * max(n, 1)))()
+    lib.bokt_splitk_reduce_sources(ntiles, split_k, nkb, launched, buf, n)
+    return [tuple(buf[3 * i:3 * i + 3]) for i in range(n)]
 
 
 _attr_cache = {}

@@ -19,9 +19,12 @@ kernels:
 * ``SPLIT_K`` 1 gives every tile one worker for its whole K loop (the
   reference's kernel, ``kernels/gemm.py:31-39``); S > 1 cuts each tile's K loop
   into S slices and deals the (tile, slice) units to the persistent CTAs in
-  contiguous runs (split-K / stream-K), the worker holding a tile's first slice
-  adding the others' fp32 partials.  Single-CTA grouped tiles or dense tiles
-  only (grouped CTA pairs are pruned).
+  contiguous runs (split-K / stream-K).  With S < 4 (and in the grouped GEMM)
+  the worker holding a tile's first slice adds the others' fp32 partials; a
+  dense GEMM with S >= 4 stores every partial and sums them in a second,
+  fully parallel kernel, so S up to 64 (tall-K shapes on all 148 SMs) stays
+  cheap.  Single-CTA grouped tiles or dense tiles only (grouped CTA pairs are
+  pruned).
 * MoE grouped GEMM only: ``RASTER`` 1 walks the tiles expert by expert; 2 spreads
   the tiles of experts with at most two 128-row blocks (weights read once or
   twice: HBM-bound) evenly between the tiles of the others (tensor-bound).
@@ -38,7 +41,7 @@ from dataclasses import asdict, dataclass
 from itertools import product
 from math import isfinite, prod
 
-SPACE_VERSION = 3
+SPACE_VERSION = 4
 KERNELS = ("gemm", "rmsnorm", "moe_grouped_gemm")
 
 
@@ -112,7 +115,12 @@ def search_space(kernel: str, profile: str = "full") -> dict[str, list[int]]:
         if profile == "full":
             space["RASTER"] = [1, 2]
             space["CTA_GROUP"] = [1, 2]
-    space["SPLIT_K"] = [1, 2, 4, 8, 16] if profile == "full" else [1, 4]
+    if profile != "full":
+        space["SPLIT_K"] = [1, 4]
+    elif kernel == "gemm":
+        space["SPLIT_K"] = [1, 2, 4, 8, 16, 32, 64]
+    else:
+        space["SPLIT_K"] = [1, 2, 4, 8, 16]
     return space
 
 

@@ -365,6 +365,38 @@ int launch_edge(const void* A, const void* B, void* C, int rows, int N, int K,
   return BOKT_OK;
 }
 
+// The separate split-K reduction after a dense launch with args.splitk_reduce
+// set: one CTA per (tile, CTA row half, 4-column group), 128 rows x `lanes`
+// worker lanes, lanes the smallest power of two (<= 8) covering the workers a
+// tile can span.
+int launch_splitk_reduce(int dtype, const TcConfig& cfg, const GemmTcArgs& args, int launched,
+                         bool pair, cudaStream_t s) {
+  const int tile_rows = pair ? 256 : 128;
+  const long long nt = (long long)((args.M + tile_rows - 1) / tile_rows) *
+                       ((args.N + cfg.bn - 1) / cfg.bn);
+  const long long blocks = nt * (pair ? 2 : 1) * (cfg.bn / 4);
+  if (blocks > 0x7fffffffLL) return fail(BOKT_ERR_UNSUPPORTED, "split-K reduction: too many tiles");
+  const int ntiles = int(nt);
+  const int workers = bokt::splitk_workers(launched, ntiles, args.split_k);
+  const int span = (workers + ntiles - 1) / ntiles + 1;  // workers one tile can touch
+  int lanes = 1;
+  while (lanes < span && lanes < bokt::kReduceMaxLanes) lanes *= 2;
+  const float* partials = reinterpret_cast<const float*>(
+      static_cast<const uint8_t*>(args.splitk_ws) + bokt::kSplitKHeaderBytes +
+      bokt::splitk_flags_bytes(args.splitk_slots));
+  cudaError_t e;
+  if (dtype == BOKT_BF16)
+    e = launch(bokt::splitk_reduce_kernel<__nv_bfloat16>, dim3(unsigned(blocks)), dim3(128 * lanes),
+               0, s, partials, static_cast<__nv_bfloat16*>(args.C), args.M, args.N, args.split_k,
+               workers, ntiles, pair ? 1 : 0, cfg.bn, args.group_m);
+  else
+    e = launch(bokt::splitk_reduce_kernel<__half>, dim3(unsigned(blocks)), dim3(128 * lanes), 0, s,
+               partials, static_cast<__half*>(args.C), args.M, args.N, args.split_k, workers,
+               ntiles, pair ? 1 : 0, cfg.bn, args.group_m);
+  if (e != cudaSuccess) return cuda_fail(e, "splitk_reduce launch");
+  return BOKT_OK;
+}
+
 bool tc_eligible(const void* A, const void* B, const void* C, int N, int K) {
   return K > 0 && (K % 8) == 0 && (N % 8) == 0 && aligned16(A) && aligned16(B) && aligned16(C);
 }
@@ -417,17 +449,25 @@ int dense_gemm_impl(const void* A, const void* B, void* C, int M, int N, int K, 
                      workspace_bytes, &args);
   if (rc) return rc;
   const long long split = args.split_k;
+  // Many slices per tile: partials summed by a separate, fully parallel
+  // kernel instead of the owner's serial fix-up (not with the fused row scale,
+  // which the owner's epilogue applies).
+  args.splitk_reduce = split >= bokt::kSplitKReduceMin && !row_scale ? 1 : 0;
   if (cfg.cta_group == 2) {
     args.idesc = bokt::make_idesc_f16(uint32_t(dtype), 256, uint32_t(cfg.bn));
     const long long units = (long long)((M + 255) / 256) * ((N + cfg.bn - 1) / cfg.bn) * split;
     const long long max_pairs = dev.sm_count / 2;
     const int pairs = int(units < max_pairs ? units : max_pairs);
-    return launch_tc2(dtype, cfg, ma, mb, args, pairs, s);
+    rc = launch_tc2(dtype, cfg, ma, mb, args, pairs, s);
+    if (rc || !args.splitk_reduce) return rc;
+    return launch_splitk_reduce(dtype, cfg, args, pairs, true, s);
   }
   args.idesc = bokt::make_idesc_f16(uint32_t(dtype), 128, uint32_t(cfg.bn));
   const long long units = (long long)((M + 127) / 128) * ((N + cfg.bn - 1) / cfg.bn) * split;
   const int grid = int(units < dev.sm_count ? units : dev.sm_count);
-  return launch_tc(false, dtype, cfg, ma, mb, args, grid, s);
+  rc = launch_tc(false, dtype, cfg, ma, mb, args, grid, s);
+  if (rc || !args.splitk_reduce) return rc;
+  return launch_splitk_reduce(dtype, cfg, args, grid, false, s);
 }
 
 // ----------------------------------------------------------------- RMSNorm dispatch
@@ -1289,6 +1329,30 @@ int bokt_splitk_schedule(int ntiles, int split_k, int nkb, int launched, int32_t
         r[5] = count;
       }
       ++n;
+    }
+  }
+  return n;
+}
+
+int bokt_splitk_reduce_sources(int ntiles, int split_k, int nkb, int launched, int32_t* out,
+                               int capacity) {
+  g_err[0] = 0;
+  if (ntiles < 0 || split_k < 1 || nkb < 1 || launched < 1 || capacity < 0 || (!out && capacity))
+    return -fail(BOKT_ERR_INVALID, "bad argument");
+  const int split = split_k < nkb ? split_k : nkb;
+  if (split <= 1) return 0;
+  const int workers = bokt::splitk_workers(launched, ntiles, split);
+  int n = 0;
+  for (int t = 0; t < ntiles; ++t) {
+    int wa, wb, first_which;
+    bokt::splitk_tile_workers(t, split, workers, ntiles, &wa, &wb, &first_which);
+    if (wb - wa < 2) continue;
+    for (int w = wa; w < wb; ++w, ++n) {
+      if (n >= capacity) continue;
+      int32_t* r = out + 3 * static_cast<int64_t>(n);
+      r[0] = t;
+      r[1] = w;
+      r[2] = w == wa ? first_which : 0;
     }
   }
   return n;

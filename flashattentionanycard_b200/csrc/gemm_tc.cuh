@@ -61,6 +61,10 @@ struct GemmTcArgs {
   int split_k;
   void* splitk_ws;
   int splitk_slots;
+  // Nonzero (dense only): every segment that does not cover its whole tile
+  // stores its partial (slot 2 c for a run's first segment, 2 c + 1 for its
+  // last; c = CTA slot) and splitk_reduce_kernel writes those tiles.
+  int splitk_reduce;
 };
 
 constexpr int kRasterExpert = 1;
@@ -417,10 +421,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
   const int split = args.split_k > 1 ? args.split_k : 1;
   SplitKView sk = {};
+  const bool fixup = split > 1 && !args.splitk_reduce;  // owner fix-up with flags
   if (split > 1) {
     sk = splitk_view(args.splitk_ws, args.splitk_slots, BN);
     // Sequence number of this launch (+1): the value the partial flags carry.
-    if (threadIdx.x == 0) tmem_holder[2] = ld_acquire_gpu(sk.header) + 1u;
+    if (fixup && threadIdx.x == 0) tmem_holder[2] = ld_acquire_gpu(sk.header) + 1u;
   }
   tc_fence_before();
   __syncthreads();
@@ -543,6 +548,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      if (args.splitk_reduce && (sg.kb0 > 0 || sg.kb1 < nkb)) {
+        // Separate reduction: only the partial; no flags, no waits.
+        epilogue_store_partial<BN>(taddr, sk.partials + slot_floats * (2 * worker + (i > 0)),
+                                   q * 32, 0, lane);
+        tc_fence_before();
+        mbar_arrive(&tempty[acc]);
+        continue;
+      }
       if (sg.kb0 > 0) {
         // Split-K non-owner: this worker's first segment; publish the fp32
         // partial rows of this warp into the CTA's slot.
@@ -588,7 +601,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // ---------------------------------------------------------------- teardown
   tc_fence_before();
   __syncthreads();
-  if (split > 1 && threadIdx.x == 0) splitk_finish(sk.header, expected);
+  if (fixup && threadIdx.x == 0) splitk_finish(sk.header, expected);
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();

@@ -117,9 +117,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // workspace slot 2 p + r for the 128 accumulator rows it holds.
   const int split = args.split_k > 1 ? args.split_k : 1;
   SplitKView sk = {};
+  const bool fixup = split > 1 && !args.splitk_reduce;  // owner fix-up with flags
   if (split > 1) {
     sk = splitk_view(args.splitk_ws, args.splitk_slots, BN);
-    if (threadIdx.x == 0) tmem_holder[2] = ld_acquire_gpu(sk.header) + 1u;
+    if (fixup && threadIdx.x == 0) tmem_holder[2] = ld_acquire_gpu(sk.header) + 1u;
   }
   tc_fence_before();
   cluster_sync();  // both CTAs' barriers initialised, TMEM allocated, schedule built
@@ -261,6 +262,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      if (args.splitk_reduce && (sg.kb0 > 0 || sg.kb1 < nkb)) {
+        // Separate reduction: only the partial (slot 2 c for the pair's first
+        // segment, 2 c + 1 for its last; c = 2 pair + rank).
+        epilogue_store_partial<BN>(taddr, sk.partials + slot_floats * (2 * my_slot + (i > 0)),
+                                   q * 32, 0, lane);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(map_shared(smem_addr(&tempty[acc]), 0));
+        continue;
+      }
       if (sg.kb0 > 0) {
         // Split-K non-owner (this pair's first segment): publish this warp's
         // fp32 partial rows into the CTA's slot.
@@ -322,7 +333,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // ---------------------------------------------------------------- teardown
   tc_fence_before();
   __syncthreads();
-  if (split > 1 && threadIdx.x == 0) splitk_finish(sk.header, expected);
+  if (fixup && threadIdx.x == 0) splitk_finish(sk.header, expected);
   cluster_sync();  // no CTA leaves while its peer may still signal its barriers
   if (warp == 1) {
     __syncwarp();

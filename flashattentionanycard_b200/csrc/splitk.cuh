@@ -34,6 +34,14 @@
 //   then          one fp32 partial tile per CTA slot: 128 rows x BN columns,
 //                 stored as [BN / 4][128 rows][4 columns] so that a warp's 32
 //                 consecutive rows of one 4-column group are 512 contiguous bytes.
+// Separate reduction (dense GEMMs with S >= kSplitKReduceMin): with many slices
+// per tile the owner's serial fix-up dominates, so instead every segment that
+// does not cover its whole tile stores its fp32 partial -- a worker's first
+// segment into its slot 2 c, its last into 2 c + 1 (c = CTA slot) -- without
+// flags or waits, and splitk_reduce_kernel, launched right after on the same
+// stream, sums each split tile's partials in worker order across all SMs and
+// writes C.  Tiles a single worker covers are written by the GEMM directly.
+//
 // A flag holds the sequence number (+1) of the launch that filled the slot, so
 // no flag has to be cleared between launches: each launch reads the sequence
 // number when it starts and the last CTA to finish advances it.  Launches that
@@ -45,7 +53,9 @@
 
 namespace bokt {
 
-constexpr int kSplitKMax = 32;
+constexpr int kSplitKMax = 128;
+// Dense GEMMs with at least this many slices use the separate reduction.
+constexpr int kSplitKReduceMin = 4;
 constexpr int kSplitKHeaderBytes = 256;
 constexpr uint64_t kSplitKWaitNs = 2000000000ull;
 
@@ -53,8 +63,10 @@ __host__ __device__ inline int64_t splitk_flags_bytes(int slots) {
   return ((int64_t(slots) * 4 * 4 + 255) / 256) * 256;
 }
 
+// Two partial tiles per CTA slot: the owner fix-up uses the first; the
+// separate reduction uses both (a worker's first and last segments).
 __host__ __device__ inline int64_t splitk_workspace_bytes(int slots, int bn) {
-  return kSplitKHeaderBytes + splitk_flags_bytes(slots) + int64_t(slots) * 128 * bn * 4;
+  return kSplitKHeaderBytes + splitk_flags_bytes(slots) + 2 * int64_t(slots) * 128 * bn * 4;
 }
 
 // A stretch of one tile's k-blocks processed by one worker.
@@ -269,6 +281,110 @@ __device__ __forceinline__ void splitk_finish(uint32_t* header, uint32_t expecte
     header[1] = 0;
     __threadfence();
     atomicExch(&header[0], expected);  // expected = sequence + 1
+  }
+}
+
+// Tile origin of output tile t in the GROUP_M raster of kernels/gemm.py:20-26
+// (the order both dense kernels walk), tiles of tile_rows x bn.
+__device__ __forceinline__ void raster_origin(int t, int M, int tile_rows, int nn, int group_m,
+                                              int bn, int* row0, int* col0) {
+  const int nm = (M + tile_rows - 1) / tile_rows;
+  const int per_group = group_m * nn;
+  const int group = t / per_group;
+  const int first_m = group * group_m;
+  const int gm = min(nm - first_m, group_m);
+  const int local = t - group * per_group;
+  *row0 = (first_m + local % gm) * tile_rows;
+  *col0 = (local / gm) * bn;
+}
+
+// Worker whose run contains unit u (run starts are non-decreasing in w).
+__host__ __device__ inline int splitk_worker_of(long long u, int workers, long long units) {
+  int w = static_cast<int>(u * workers / units);
+  if (w >= workers) w = workers - 1;
+  while (w + 1 < workers && splitk_run_start(w + 1, workers, units) <= u) ++w;
+  while (w > 0 && splitk_run_start(w, workers, units) > u) --w;
+  return w;
+}
+
+// Separate reduction: the workers [*wa, *wb) whose runs hold units of tile t,
+// and which of wa's two partial slots holds the tile (*first_which: 1 when the
+// tile is the last segment of a run that started in an earlier tile, else 0;
+// every later worker's run starts inside the tile, so the tile is its first
+// segment, slot 0).  *wb - *wa < 2: one worker covered the tile, no partials.
+__host__ __device__ inline void splitk_tile_workers(int t, int split, int workers, int ntiles,
+                                                    int* wa, int* wb, int* first_which) {
+  const long long units = static_cast<long long>(ntiles) * split;
+  const long long u0 = static_cast<long long>(t) * split;
+  *wa = splitk_worker_of(u0, workers, units);
+  *wb = splitk_worker_of(u0 + split - 1, workers, units) + 1;
+  *first_which = splitk_run_start(*wa, workers, units) < u0 ? 1 : 0;
+}
+
+// Threads per (tile, CTA row half, 4-column group): 128 rows x `lanes` worker
+// lanes, lanes in {1, 2, 4, 8}.
+constexpr int kReduceMaxLanes = 8;
+
+// The separate split-K reduction.  CTA (tile t, CTA row half h, column group
+// g): rows 128 h .. 128 h + 127 of the tile (h = 0 for single-CTA tiles),
+// columns 4 g .. 4 g + 3.  Thread (lane p, row r) sums, in worker order, the
+// partials of the tile's workers wa + p, wa + p + lanes, ...; lane 0 then adds
+// the lanes' sums in lane order and stores the row's 4 outputs, rounded once.
+// The order depends only on the shape and the launch, so repeated runs are
+// bit-identical.  Tiles a single worker covered are skipped (the GEMM wrote
+// them).
+template <typename T>
+__global__ void __launch_bounds__(128 * kReduceMaxLanes) splitk_reduce_kernel(
+    const float* __restrict__ partials, T* __restrict__ C, int M, int N, int split, int workers,
+    int ntiles, int pair, int bn, int group_m) {
+  __shared__ float4 lane_sum[kReduceMaxLanes - 1][128];
+  pdl_allow_next();
+  pdl_wait();
+  const int halves = pair ? 2 : 1;
+  const int groups = bn / 4;
+  int id = blockIdx.x;
+  const int g = id % groups;
+  id /= groups;
+  const int h = id % halves;
+  const int t = id / halves;
+  const int lanes = blockDim.x / 128;
+  const int r = threadIdx.x & 127;
+  const int p = threadIdx.x >> 7;
+  int wa, wb, first_which;
+  splitk_tile_workers(t, split, workers, ntiles, &wa, &wb, &first_which);
+  if (wb - wa < 2) return;  // whole tile on one worker
+  const int64_t slot_floats = static_cast<int64_t>(128) * bn;
+  const float4* base = reinterpret_cast<const float4*>(partials) + static_cast<size_t>(g) * 128 + r;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+  for (int w = wa + p; w < wb; w += lanes) {
+    const int cta = pair ? 2 * w + h : w;
+    const int which = w == wa ? first_which : 0;
+    const float4 f = __ldcg(base + (slot_floats / 4) * (2 * cta + which));
+    acc.x += f.x;
+    acc.y += f.y;
+    acc.z += f.z;
+    acc.w += f.w;
+  }
+  if (p > 0) lane_sum[p - 1][r] = acc;
+  __syncthreads();
+  if (p > 0) return;
+  for (int j = 1; j < lanes; ++j) {
+    const float4 f = lane_sum[j - 1][r];
+    acc.x += f.x;
+    acc.y += f.y;
+    acc.z += f.z;
+    acc.w += f.w;
+  }
+  int row0, col0;
+  raster_origin(t, M, pair ? 256 : 128, (N + bn - 1) / bn, group_m, bn, &row0, &col0);
+  const int row = row0 + 128 * h + r;
+  const int col = col0 + 4 * g;
+  if (row < M && col < N) {
+    uint2 o;
+    o.x = Pack2<T>::pack(acc.x, acc.y);
+    o.y = Pack2<T>::pack(acc.z, acc.w);
+    *reinterpret_cast<uint2*>(C + static_cast<size_t>(row) * N + col) = o;
   }
 }
 

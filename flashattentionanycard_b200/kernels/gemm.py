@@ -8,7 +8,8 @@ row-major contiguous, result rounded to ``out``'s dtype, every element of
 ``SPLIT_K`` > 1 the K loop of every tile is split across workers (split-K /
 stream-K); the fp32 partials go through a per-device workspace allocated on
 the first such call (``_native.splitk_workspace``), so that first call must
-come before any graph capture.
+come before any graph capture.  From ``SPLIT_K`` 4 up the partials are summed
+by a second kernel launched right after the GEMM on the same stream.
 """
 
 import ctypes

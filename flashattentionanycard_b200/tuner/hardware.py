@@ -20,6 +20,7 @@ from dataclasses import asdict, dataclass, field
 GEMM_BM, GEMM_BK = 128, 64
 GEMM_WARPS = 6
 TMEM_COLUMNS = 512
+SPLIT_K_MAX = 128  # slices per tile the library accepts (kSplitKMax)
 EPILOGUE_BYTES = 4 * (32 * 128 + 32 * 8)  # staging + row pointers of the 4 epilogue warps
 
 
@@ -182,7 +183,7 @@ def prune_reason(hardware, kernel, params, columns=0, heuristic_smem=False):
     if pair and params["BLOCK_N"] == 64:
         return "illegal_tile_shape"
     split = params.get("SPLIT_K", 1)
-    if split < 1 or split > 32 or (split > 1 and pair and kernel == "moe_grouped_gemm"):
+    if split < 1 or split > SPLIT_K_MAX or (split > 1 and pair and kernel == "moe_grouped_gemm"):
         return "illegal_split_k"
     experts = 64 if kernel == "moe_grouped_gemm" else 0
     smem = (gemm_pair_shared_bytes(params["BLOCK_N"], params["num_stages"], experts) if pair

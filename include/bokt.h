@@ -128,14 +128,18 @@ int bokt_gemm(const void* A, const void* B, void* C, int M, int N, int K, int dt
  * the number of 64-wide k-blocks) and deals the (tile, slice) units out to the
  * persistent CTAs (or CTA pairs) in contiguous runs, so every worker gets the
  * same number of k-block iterations even when the tile count is not a multiple
- * of the SM count; S = number of k-blocks is stream-K.  The worker that holds a
- * tile's first slice adds the other workers' fp32 partial tiles (read from the
- * workspace, in worker order: deterministic) and writes C.  The K loop being
+ * of the SM count; S = number of k-blocks is stream-K.  S in [1, 128].  For
+ * S < 4 the worker that holds a tile's first slice adds the other workers'
+ * fp32 partial tiles (read from the workspace, in worker order:
+ * deterministic) and writes C.  For S >= 4 (without a row scale) every worker
+ * stores the partials of the tiles it does not cover whole and a second
+ * kernel, launched on the same stream right after, sums each split tile's
+ * partials (fixed order: deterministic) and writes C.  The K loop being
  * split is the one of kernels/gemm.py:31-39 in the reference; the parameter is
  * the split-K entry of the redefined search space (configs/search_spaces.py:48-75).
  *
  * workspace: device memory of bokt_gemm_workspace_bytes(BOKT_KERNEL_GEMM,
- * params) bytes (about 19 MB at block_n 256 on a 148-SM B200), 256-byte
+ * params) bytes (about 39 MB at block_n 256 on a 148-SM B200), 256-byte
  * aligned and zero-filled ONCE when it is allocated; the library keeps a
  * launch sequence number in it, so it is not cleared between calls.  Calls
  * that share a workspace must not overlap on the GPU (use one per stream).
@@ -161,6 +165,17 @@ int64_t bokt_gemm_workspace_bytes(int kernel, const bokt_params* params);
  */
 int bokt_splitk_schedule(int ntiles, int split_k, int nkb, int launched, int32_t* out,
                          int capacity);
+
+/*
+ * Sources of the separate split-K reduction (dense GEMMs with split_k >= 4):
+ * for every tile split across workers, in tile order and then in the order
+ * the reduction adds them, the triple (tile, worker, which) -- the partial in
+ * workspace slot 2 c + which of the worker's CTA slot c (a pair worker p owns
+ * CTA slots 2 p and 2 p + 1).  Same arguments and return convention as
+ * bokt_splitk_schedule; the kernels' own arithmetic, run on the host.
+ */
+int bokt_splitk_reduce_sources(int ntiles, int split_k, int nkb, int launched, int32_t* out,
+                               int capacity);
 
 /*
  * Y[M,N] = X * rsqrt(mean(X^2, -1) + eps) * W, fp32 arithmetic, one pass over X.

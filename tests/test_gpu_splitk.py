@@ -79,11 +79,53 @@ def test_dense_split_ragged(shape, dtype, cuda_device):
             gate(out, ref, dtype)
 
 
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+@pytest.mark.parametrize("shape", [(256, 256, 65536), (128, 512, 32768), (300, 136, 20000)])
+def test_dense_split_tall_k(shape, dtype, cuda_device):
+    """Tall-K shapes (one to a few output tiles, hundreds of k-blocks) with
+    the separate reduction, up to 128 slices: single CTAs and pairs, every
+    split tile summed from up to 148 partials; repeated runs bit-identical."""
+    m, n, k = shape
+    a, b = _inputs(m, n, k, dtype, m + n)
+    ref = numerics.gemm_fp32(as_f32(a), as_f32(b))
+    a, b = a.to(cuda_device), b.to(cuda_device)
+    for cta_group in (1, 2):
+        for split in (4, 16, 64, 128):
+            p = {"BLOCK_N": 128 if n % 256 else 256, "CTA_GROUP": cta_group, "SPLIT_K": split}
+            outs = []
+            for _ in range(2):
+                out = nan_like((m, n), dtype, cuda_device)
+                gemm.launch(a, b, out, p)
+                torch.cuda.synchronize()
+                outs.append(out)
+            gate(outs[0], ref, dtype)
+            assert torch.equal(outs[0], outs[1]), f"split {split} differs between identical runs"
+
+
+def test_owner_fixup_and_separate_reduction_agree(cuda_device):
+    """S = 3 (owner fix-up) and S = 4 (separate reduction) of one problem both
+    pass the gate and agree to within a rounding step almost everywhere."""
+    a, b = _inputs(512, 768, 8192, "bf16", 5)
+    ref = numerics.gemm_fp32(as_f32(a), as_f32(b))
+    a, b = a.to(cuda_device), b.to(cuda_device)
+    outs = []
+    for split in (3, 4):
+        out = nan_like((512, 768), "bf16", cuda_device)
+        gemm.launch(a, b, out, {"CTA_GROUP": 2, "SPLIT_K": split})
+        torch.cuda.synchronize()
+        gate(out, ref, "bf16")
+        outs.append(out.float())
+    diff = (outs[0] - outs[1]).abs()
+    assert float((diff > outs[0].abs() * 2.0 ** -7 + 1e-6).float().mean()) < 1e-3
+
+
 def test_split_graph_replay_and_shared_workspace(cuda_device):
-    """Back-to-back split launches of two shapes share one workspace inside a
-    CUDA graph replayed many times (the launch sequence number, not a cleared
-    flag, tells a fresh partial from a stale one)."""
-    shapes = [(2048, 2048, 2048, 8), (512, 1024, 3072, 16)]
+    """Back-to-back split launches of four shapes (owner fix-up and separate
+    reduction) share one workspace inside a CUDA graph replayed many times
+    (the launch sequence number, not a cleared flag, tells a fresh partial
+    from a stale one; a reduction finishes before the next GEMM writes)."""
+    shapes = [(2048, 2048, 2048, 8), (512, 1024, 3072, 16), (1024, 1024, 2048, 2),
+              (256, 256, 32768, 64)]
     data = []
     for m, n, k, s in shapes:
         a, b = _inputs(m, n, k, "bf16", m + k)

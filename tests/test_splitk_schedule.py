@@ -59,3 +59,55 @@ def test_stream_k_2048_pairs():
         per[w] = per.get(w, 0) + (k1 - k0)
     assert len(per) == 74 and max(per.values()) == 28 and min(per.values()) == 24
     assert segs[0] == (0, 0, 0, 24, 1, 1)
+
+
+def _written_partials(ntiles, split, nkb, launched):
+    """(tile, worker, which) of every partial the GEMM epilogue stores in the
+    separate-reduction mode: a segment that does not cover its whole tile goes
+    to slot 0 when it is the first of its worker's run, else slot 1."""
+    out = {}
+    index = {}
+    for w, t, k0, k1, _, _ in _native.splitk_schedule(ntiles, split, nkb, launched):
+        i = index.get(w, 0)
+        index[w] = i + 1
+        if k0 > 0 or k1 < nkb:
+            key = (w, 1 if i > 0 else 0)
+            assert key not in out, "two partials written into one slot"
+            out[key] = (t, k0, k1)
+    return out
+
+
+@pytest.mark.parametrize("ntiles", [1, 2, 3, 16, 64, 120, 1024])
+def test_reduce_sources_match_written_partials(ntiles):
+    """Every partial the reduction reads was written for that tile, every
+    written partial is read exactly once, and per tile the reads run in worker
+    order over k-blocks 0 .. nkb without gaps."""
+    checked = 0
+    for split, nkb, launched in itertools.product((4, 5, 16, 64, 128), (4, 16, 65, 1024),
+                                                  (1, 5, 74, 148)):
+        written = _written_partials(ntiles, split, nkb, launched)
+        sources = _native.splitk_reduce_sources(ntiles, split, nkb, launched)
+        seen = set()
+        by_tile = {}
+        for t, w, which in sources:
+            assert which in (0, 1)
+            assert (w, which) in written, "reduction reads a slot nothing wrote"
+            assert written[(w, which)][0] == t, "slot holds another tile's partial"
+            assert (w, which) not in seen
+            seen.add((w, which))
+            by_tile.setdefault(t, []).append(written[(w, which)])
+        assert seen == set(written), "a written partial is never read"
+        for t, parts in by_tile.items():
+            assert len(parts) >= 2
+            assert parts[0][1] == 0 and parts[-1][2] == nkb
+            assert all(a[2] == b[1] for a, b in zip(parts, parts[1:]))
+        checked += len(sources)
+    assert checked > 0
+
+
+def test_reduce_tall_k_pairs():
+    """256 x 256 x 65536 on 74 pairs with 64 slices: the single tile is summed
+    from the partials of all 64 workers."""
+    sources = _native.splitk_reduce_sources(1, 64, 1024, 74)
+    assert [w for _, w, _ in sources] == list(range(64))
+    assert all(which == 0 for *_, which in sources)
