@@ -366,33 +366,43 @@ int launch_edge(const void* A, const void* B, void* C, int rows, int N, int K,
 }
 
 // The separate split-K reduction after a dense launch with args.splitk_reduce
-// set: one CTA per (tile, CTA row half, 4-column group), 128 rows x `lanes`
-// worker lanes, lanes the smallest power of two (<= 8) covering the workers a
-// tile can span.
+// set: one CTA per (tile, CTA row half, 16 / lanes column groups of 4),
+// 128 rows x `lanes` worker lanes; lanes grows with the workers one tile can
+// span (about four partials per lane, at most 8 lanes).
 int launch_splitk_reduce(int dtype, const TcConfig& cfg, const GemmTcArgs& args, int launched,
                          bool pair, cudaStream_t s) {
   const int tile_rows = pair ? 256 : 128;
   const long long nt = (long long)((args.M + tile_rows - 1) / tile_rows) *
                        ((args.N + cfg.bn - 1) / cfg.bn);
-  const long long blocks = nt * (pair ? 2 : 1) * (cfg.bn / 4);
-  if (blocks > 0x7fffffffLL) return fail(BOKT_ERR_UNSUPPORTED, "split-K reduction: too many tiles");
   const int ntiles = int(nt);
   const int workers = bokt::splitk_workers(launched, ntiles, args.split_k);
   const int span = (workers + ntiles - 1) / ntiles + 1;  // workers one tile can touch
   int lanes = 1;
-  while (lanes < span && lanes < bokt::kReduceMaxLanes) lanes *= 2;
+  while (lanes * 4 < span && lanes < 8) lanes *= 2;
+  const long long blocks = nt * (pair ? 2 : 1) * (cfg.bn / (64 / lanes));
+  if (blocks > 0x7fffffffLL) return fail(BOKT_ERR_UNSUPPORTED, "split-K reduction: too many tiles");
   const float* partials = reinterpret_cast<const float*>(
       static_cast<const uint8_t*>(args.splitk_ws) + bokt::kSplitKHeaderBytes +
       bokt::splitk_flags_bytes(args.splitk_slots));
-  cudaError_t e;
-  if (dtype == BOKT_BF16)
-    e = launch(bokt::splitk_reduce_kernel<__nv_bfloat16>, dim3(unsigned(blocks)), dim3(128 * lanes),
-               0, s, partials, static_cast<__nv_bfloat16*>(args.C), args.M, args.N, args.split_k,
-               workers, ntiles, pair ? 1 : 0, cfg.bn, args.group_m);
-  else
-    e = launch(bokt::splitk_reduce_kernel<__half>, dim3(unsigned(blocks)), dim3(128 * lanes), 0, s,
-               partials, static_cast<__half*>(args.C), args.M, args.N, args.split_k, workers,
-               ntiles, pair ? 1 : 0, cfg.bn, args.group_m);
+  const int p = pair ? 1 : 0;
+  cudaError_t e = cudaSuccess;
+  auto go = [&](auto kernel, auto* c) {
+    e = launch(kernel, dim3(unsigned(blocks)), dim3(128 * lanes), 0, s, partials, c, args.M,
+               args.N, args.split_k, workers, ntiles, p, cfg.bn, args.group_m);
+  };
+  if (dtype == BOKT_BF16) {
+    auto* c = static_cast<__nv_bfloat16*>(args.C);
+    if (lanes == 1) go(bokt::splitk_reduce_kernel<__nv_bfloat16, 1>, c);
+    else if (lanes == 2) go(bokt::splitk_reduce_kernel<__nv_bfloat16, 2>, c);
+    else if (lanes == 4) go(bokt::splitk_reduce_kernel<__nv_bfloat16, 4>, c);
+    else go(bokt::splitk_reduce_kernel<__nv_bfloat16, 8>, c);
+  } else {
+    auto* c = static_cast<__half*>(args.C);
+    if (lanes == 1) go(bokt::splitk_reduce_kernel<__half, 1>, c);
+    else if (lanes == 2) go(bokt::splitk_reduce_kernel<__half, 2>, c);
+    else if (lanes == 4) go(bokt::splitk_reduce_kernel<__half, 4>, c);
+    else go(bokt::splitk_reduce_kernel<__half, 8>, c);
+  }
   if (e != cudaSuccess) return cuda_fail(e, "splitk_reduce launch");
   return BOKT_OK;
 }

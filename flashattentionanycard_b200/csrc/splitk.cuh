@@ -298,13 +298,11 @@ __device__ __forceinline__ void raster_origin(int t, int M, int tile_rows, int n
   *col0 = (local / gm) * bn;
 }
 
-// Worker whose run contains unit u (run starts are non-decreasing in w).
+// Worker whose run contains unit u: the largest w with
+// floor(units w / workers) <= u, i.e. units w < (u + 1) workers.
 __host__ __device__ inline int splitk_worker_of(long long u, int workers, long long units) {
-  int w = static_cast<int>(u * workers / units);
-  if (w >= workers) w = workers - 1;
-  while (w + 1 < workers && splitk_run_start(w + 1, workers, units) <= u) ++w;
-  while (w > 0 && splitk_run_start(w, workers, units) > u) --w;
-  return w;
+  const long long w = ((u + 1) * workers - 1) / units;
+  return w < workers ? static_cast<int>(w) : workers - 1;
 }
 
 // Separate reduction: the workers [*wa, *wb) whose runs hold units of tile t,
@@ -321,70 +319,98 @@ __host__ __device__ inline void splitk_tile_workers(int t, int split, int worker
   *first_which = splitk_run_start(*wa, workers, units) < u0 ? 1 : 0;
 }
 
-// Threads per (tile, CTA row half, 4-column group): 128 rows x `lanes` worker
-// lanes, lanes in {1, 2, 4, 8}.
-constexpr int kReduceMaxLanes = 8;
-
-// The separate split-K reduction.  CTA (tile t, CTA row half h, column group
-// g): rows 128 h .. 128 h + 127 of the tile (h = 0 for single-CTA tiles),
-// columns 4 g .. 4 g + 3.  Thread (lane p, row r) sums, in worker order, the
-// partials of the tile's workers wa + p, wa + p + lanes, ...; lane 0 then adds
-// the lanes' sums in lane order and stores the row's 4 outputs, rounded once.
-// The order depends only on the shape and the launch, so repeated runs are
-// bit-identical.  Tiles a single worker covered are skipped (the GEMM wrote
-// them).
-template <typename T>
-__global__ void __launch_bounds__(128 * kReduceMaxLanes) splitk_reduce_kernel(
+// The separate split-K reduction.  CTA (tile t, CTA row half h, chunk c):
+// rows 128 h .. 128 h + 127 of the tile (h = 0 for single-CTA tiles) and the
+// 16 / LANES 4-column groups of chunk c.  Thread (lane p, row r) sums, in
+// worker order, the partials of workers wa + p, wa + p + LANES, ... of the
+// tile for each of the chunk's groups (independent accumulators: many loads
+// in flight); lane 0 adds the lanes' sums in lane order, rounds once and
+// stores the row's 64 / LANES outputs.  LANES splits the workers of tiles that
+// many workers share (tall K); with few workers per tile one lane keeps all
+// 16 groups.  The order depends only on the shape and the launch, so repeated
+// runs are bit-identical.  Tiles a single worker covered are skipped (the GEMM
+// wrote them).  One thread derives the tile's workers and origin (schedule
+// arithmetic, no memory reads) before the wait on the GEMM.
+template <typename T, int LANES>
+__global__ void __launch_bounds__(128 * LANES) splitk_reduce_kernel(
     const float* __restrict__ partials, T* __restrict__ C, int M, int N, int split, int workers,
     int ntiles, int pair, int bn, int group_m) {
-  __shared__ float4 lane_sum[kReduceMaxLanes - 1][128];
+  constexpr int G = 16 / LANES;  // 4-column groups per CTA
+  __shared__ float4 lane_sum[LANES > 1 ? LANES - 1 : 1][LANES > 1 ? G : 1][128];
+  __shared__ int info[5];  // wa, wb, first_which, row0, col0
   pdl_allow_next();
-  pdl_wait();
   const int halves = pair ? 2 : 1;
-  const int groups = bn / 4;
+  const int chunks = bn / (4 * G);
   int id = blockIdx.x;
-  const int g = id % groups;
-  id /= groups;
+  const int c = id % chunks;
+  id /= chunks;
   const int h = id % halves;
   const int t = id / halves;
-  const int lanes = blockDim.x / 128;
+  if (threadIdx.x == 0) {
+    splitk_tile_workers(t, split, workers, ntiles, &info[0], &info[1], &info[2]);
+    raster_origin(t, M, pair ? 256 : 128, (N + bn - 1) / bn, group_m, bn, &info[3], &info[4]);
+  }
+  __syncthreads();
+  const int wa = info[0], wb = info[1], first_which = info[2];
+  // Every CTA waits, also one that has nothing to do: the next kernel's wait
+  // covers this grid only, so this grid must not finish before the GEMM.
+  pdl_wait();
+  if (wb - wa < 2) return;  // whole tile on one worker
   const int r = threadIdx.x & 127;
   const int p = threadIdx.x >> 7;
-  int wa, wb, first_which;
-  splitk_tile_workers(t, split, workers, ntiles, &wa, &wb, &first_which);
-  if (wb - wa < 2) return;  // whole tile on one worker
-  const int64_t slot_floats = static_cast<int64_t>(128) * bn;
-  const float4* base = reinterpret_cast<const float4*>(partials) + static_cast<size_t>(g) * 128 + r;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-  for (int w = wa + p; w < wb; w += lanes) {
+  const int64_t slot_vecs = static_cast<int64_t>(32) * bn;  // float4s per partial tile
+  const float4* base =
+      reinterpret_cast<const float4*>(partials) + static_cast<size_t>(c) * G * 128 + r;
+  float4 acc[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int w = wa + p; w < wb; w += LANES) {
     const int cta = pair ? 2 * w + h : w;
-    const int which = w == wa ? first_which : 0;
-    const float4 f = __ldcg(base + (slot_floats / 4) * (2 * cta + which));
-    acc.x += f.x;
-    acc.y += f.y;
-    acc.z += f.z;
-    acc.w += f.w;
+    const float4* src = base + slot_vecs * (2 * cta + (w == wa ? first_which : 0));
+    float4 f[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) f[g] = __ldcg(src + g * 128);
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      acc[g].x += f[g].x;
+      acc[g].y += f[g].y;
+      acc[g].z += f[g].z;
+      acc[g].w += f[g].w;
+    }
   }
-  if (p > 0) lane_sum[p - 1][r] = acc;
-  __syncthreads();
-  if (p > 0) return;
-  for (int j = 1; j < lanes; ++j) {
-    const float4 f = lane_sum[j - 1][r];
-    acc.x += f.x;
-    acc.y += f.y;
-    acc.z += f.z;
-    acc.w += f.w;
+  if constexpr (LANES > 1) {
+    if (p > 0) {
+#pragma unroll
+      for (int g = 0; g < G; ++g) lane_sum[p - 1][g][r] = acc[g];
+    }
+    __syncthreads();
+    if (p > 0) return;
+    for (int j = 1; j < LANES; ++j) {
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float4 f = lane_sum[j - 1][g][r];
+        acc[g].x += f.x;
+        acc[g].y += f.y;
+        acc[g].z += f.z;
+        acc[g].w += f.w;
+      }
+    }
   }
-  int row0, col0;
-  raster_origin(t, M, pair ? 256 : 128, (N + bn - 1) / bn, group_m, bn, &row0, &col0);
-  const int row = row0 + 128 * h + r;
-  const int col = col0 + 4 * g;
-  if (row < M && col < N) {
-    uint2 o;
-    o.x = Pack2<T>::pack(acc.x, acc.y);
-    o.y = Pack2<T>::pack(acc.z, acc.w);
-    *reinterpret_cast<uint2*>(C + static_cast<size_t>(row) * N + col) = o;
+  const int row = info[3] + 128 * h + r;
+  const int col = info[4] + 4 * G * c;
+  if (row >= M) return;
+  T* out = C + static_cast<size_t>(row) * N + col;
+  // 8 columns (16 bytes) at a time; N is a multiple of 8 on this path.
+#pragma unroll
+  for (int g = 0; g < G; g += 2) {
+    if (col + 4 * g < N) {
+      uint4 o;
+      o.x = Pack2<T>::pack(acc[g].x, acc[g].y);
+      o.y = Pack2<T>::pack(acc[g].z, acc[g].w);
+      o.z = Pack2<T>::pack(acc[g + 1].x, acc[g + 1].y);
+      o.w = Pack2<T>::pack(acc[g + 1].z, acc[g + 1].w);
+      *reinterpret_cast<uint4*>(out + 4 * g) = o;
+    }
   }
 }
 
