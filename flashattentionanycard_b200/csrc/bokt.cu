@@ -366,7 +366,7 @@ int launch_edge(const void* A, const void* B, void* C, int rows, int N, int K,
 }
 
 // The separate split-K reduction after a dense launch with args.splitk_reduce
-// set: one CTA per (tile, CTA row half, 16 / lanes column groups of 4),
+// set: one CTA per (tile, CTA row half, 8 / lanes column groups of 4),
 // 128 rows x `lanes` worker lanes; lanes grows with the workers one tile can
 // span (about four partials per lane, at most 8 lanes).
 int launch_splitk_reduce(int dtype, const TcConfig& cfg, const GemmTcArgs& args, int launched,
@@ -379,7 +379,7 @@ int launch_splitk_reduce(int dtype, const TcConfig& cfg, const GemmTcArgs& args,
   const int span = (workers + ntiles - 1) / ntiles + 1;  // workers one tile can touch
   int lanes = 1;
   while (lanes * 4 < span && lanes < 8) lanes *= 2;
-  const long long blocks = nt * (pair ? 2 : 1) * (cfg.bn / (64 / lanes));
+  const long long blocks = nt * (pair ? 2 : 1) * (cfg.bn / (32 / lanes));
   if (blocks > 0x7fffffffLL) return fail(BOKT_ERR_UNSUPPORTED, "split-K reduction: too many tiles");
   const float* partials = reinterpret_cast<const float*>(
       static_cast<const uint8_t*>(args.splitk_ws) + bokt::kSplitKHeaderBytes +

@@ -321,13 +321,13 @@ __host__ __device__ inline void splitk_tile_workers(int t, int split, int worker
 
 // The separate split-K reduction.  CTA (tile t, CTA row half h, chunk c):
 // rows 128 h .. 128 h + 127 of the tile (h = 0 for single-CTA tiles) and the
-// 16 / LANES 4-column groups of chunk c.  Thread (lane p, row r) sums, in
+// G = 8 / LANES 4-column groups of chunk c.  Thread (lane p, row r) sums, in
 // worker order, the partials of workers wa + p, wa + p + LANES, ... of the
 // tile for each of the chunk's groups (independent accumulators: many loads
 // in flight); lane 0 adds the lanes' sums in lane order, rounds once and
-// stores the row's 64 / LANES outputs.  LANES splits the workers of tiles that
-// many workers share (tall K); with few workers per tile one lane keeps all
-// 16 groups.  The order depends only on the shape and the launch, so repeated
+// stores the row's 4 G outputs.  LANES splits the workers of tiles that many
+// workers share (tall K: few tiles, so also narrow chunks for more CTAs); with
+// few workers per tile one lane keeps 8 groups.  The order depends only on the shape and the launch, so repeated
 // runs are bit-identical.  Tiles a single worker covered are skipped (the GEMM
 // wrote them).  One thread derives the tile's workers and origin (schedule
 // arithmetic, no memory reads) before the wait on the GEMM.
@@ -335,7 +335,7 @@ template <typename T, int LANES>
 __global__ void __launch_bounds__(128 * LANES) splitk_reduce_kernel(
     const float* __restrict__ partials, T* __restrict__ C, int M, int N, int split, int workers,
     int ntiles, int pair, int bn, int group_m) {
-  constexpr int G = 16 / LANES;  // 4-column groups per CTA
+  constexpr int G = 8 / LANES;  // 4-column groups per CTA
   __shared__ float4 lane_sum[LANES > 1 ? LANES - 1 : 1][LANES > 1 ? G : 1][128];
   __shared__ int info[5];  // wa, wb, first_which, row0, col0
   pdl_allow_next();
@@ -400,16 +400,25 @@ __global__ void __launch_bounds__(128 * LANES) splitk_reduce_kernel(
   const int col = info[4] + 4 * G * c;
   if (row >= M) return;
   T* out = C + static_cast<size_t>(row) * N + col;
-  // 8 columns (16 bytes) at a time; N is a multiple of 8 on this path.
+  if constexpr (G == 1) {
+    if (col < N) {  // N is a multiple of 8 on this path, col of 4
+      uint2 o;
+      o.x = Pack2<T>::pack(acc[0].x, acc[0].y);
+      o.y = Pack2<T>::pack(acc[0].z, acc[0].w);
+      *reinterpret_cast<uint2*>(out) = o;
+    }
+  } else {
+    // 8 columns (16 bytes) at a time; N is a multiple of 8 on this path.
 #pragma unroll
-  for (int g = 0; g < G; g += 2) {
-    if (col + 4 * g < N) {
-      uint4 o;
-      o.x = Pack2<T>::pack(acc[g].x, acc[g].y);
-      o.y = Pack2<T>::pack(acc[g].z, acc[g].w);
-      o.z = Pack2<T>::pack(acc[g + 1].x, acc[g + 1].y);
-      o.w = Pack2<T>::pack(acc[g + 1].z, acc[g + 1].w);
-      *reinterpret_cast<uint4*>(out + 4 * g) = o;
+    for (int g = 0; g < G; g += 2) {
+      if (col + 4 * g < N) {
+        uint4 o;
+        o.x = Pack2<T>::pack(acc[g].x, acc[g].y);
+        o.y = Pack2<T>::pack(acc[g].z, acc[g].w);
+        o.z = Pack2<T>::pack(acc[g + 1].x, acc[g + 1].y);
+        o.w = Pack2<T>::pack(acc[g + 1].z, acc[g + 1].w);
+        *reinterpret_cast<uint4*>(out + 4 * g) = o;
+      }
     }
   }
 }
