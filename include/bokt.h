@@ -86,7 +86,7 @@ typedef struct bokt_params {
   int32_t cta_multiplier;
   int32_t num_warps;
   int32_t rows_per_cta;
-  int32_t split_k;   /* 0/1: one worker runs a tile's whole K loop; 2..32: split-K /
+  int32_t split_k;   /* 0/1: one worker runs a tile's whole K loop; 2..128: split-K /
                         stream-K (see bokt_gemm_ex); needs a workspace */
   int32_t cta_group; /* 0/1: one CTA per tile; 2: CTA pairs (dense GEMM) */
   int32_t raster;    /* grouped GEMM tile order: 0/1 expert order, 2 balanced
