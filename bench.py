@@ -33,8 +33,9 @@ torch fp32 computation on the device, TF32 off, with the reference's gate
 tolerances) and reports ``parity``; a mismatch makes the run exit non-zero.
 Inputs are larger than L2 (126 MB) or rotated through buffer sets that
 together exceed it, so every step reads from HBM.  ``--impl reference`` times
-the reference's FP32 CPU path (the oracle port, numpy) on the host cores with
-the same ``config`` dicts.
+the reference's FP32 CPU path (its worker's torch expressions on CPU tensors,
+restated in ``oracle/reference_cpu.py``) on the host cores with the same
+``config`` dicts.
 """
 
 import argparse
@@ -47,7 +48,6 @@ import subprocess
 import sys
 import threading
 import time
-from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 REPO = Path(__file__).resolve().parent
@@ -1061,105 +1061,95 @@ DEFAULT_STEPS = {"gemm": 200, "rmsnorm": 4000, "gemm8192": 200, "gemm2048": 2000
 
 # ----------------------------------------------------------------------------- CPU reference
 class CpuLeg:
-    """The reference's FP32 CPU path (oracle port, numpy/BLAS) of one workload,
-    on a bounded sample; ``step`` returns the work done (bytes or FLOPs)."""
+    """The reference's FP32 CPU path of one workload: its own torch expressions
+    (oracle.reference_cpu, reference tuner/worker.py:64, 73-74, 88-90) on CPU
+    tensors of the 16-bit inputs, intra-op threads over the host cores, on a
+    bounded sample; ``step`` returns the work done (bytes or FLOPs)."""
 
     def __init__(self, name):
         from flashattentionanycard_b200 import workloads
 
         self.name = name
         self.unit = "GB/s" if name == "rmsnorm" else "TFLOP/s"
+        expr = "the reference's FP32 torch expression"
         if name == "rmsnorm":
             cfg = workloads.RMSNORM
             m, n, eps = cfg["m"], cfg["n"], cfg["eps"]
-            x, w = workloads.rmsnorm_inputs(m, n, "bf16", seed=0)
-            self.cx, self.cw, self.eps = x.float().numpy(), w.float().numpy(), eps
-            self.sample = "numpy fp32 RMSNorm of the full 4096x4096 input, rows split over host threads"
+            self.x, self.w = workloads.rmsnorm_inputs(m, n, "bf16", seed=0)
+            self.eps = eps
+            self.sample = f"{expr} (worker.py:73-74) on the full 4096x4096 bf16 input"
             self.work = 2 * m * n * 2 + n * 2
         elif name == "gemm":
             m, n, k = GEMM_SHAPE
             rows = min(m, 256)
-            a, b = workloads.gemm_inputs(rows, n, k, "bf16", seed=0)
-            self.ca, self.cb = a.float().numpy(), b.float().numpy()
-            self.sample = f"numpy/BLAS fp32 GEMM of {rows} rows of A x B (K={k}, N={n})"
+            self.a, self.b = workloads.gemm_inputs(rows, n, k, "bf16", seed=0)
+            self.sample = f"{expr} (worker.py:64) on {rows} rows of A x B (K={k}, N={n})"
             self.work = 2.0 * rows * n * k
         elif name.startswith("gemm"):
             size = 8192 if name.startswith("gemm8192") else 2048
             dtype = "fp16" if name.endswith("_fp16") else "bf16"
             rows = 256 if size > 2048 else size
-            a, b = workloads.gemm_inputs(size, size, size, dtype, seed=0)
-            self.ca, self.cb = a[:rows].float().numpy(), b.float().numpy()
-            self.sample = f"numpy/BLAS fp32 GEMM of {rows} rows of A x B (K={size}, N={size})"
+            a, self.b = workloads.gemm_inputs(size, size, size, dtype, seed=0)
+            self.a = a[:rows].contiguous()
+            self.sample = f"{expr} (worker.py:64) on {rows} rows of A x B (K={size}, N={size})"
             self.work = 2.0 * rows * size * size
         elif name == "moe_small":
             counts = workloads.MOE_SMALL_COUNTS
             k, n = workloads.MOE_SMALL["k"], workloads.MOE_SMALL["n"]
-            x, w = workloads.moe_inputs(counts, k, n, "bf16", seed=0)
-            self.cx, self.cw = x.float().numpy(), w.float().numpy()
-            self.cstarts = workloads.offsets_from_counts(counts)
-            self.sample = "numpy/BLAS fp32 per-expert GEMMs of the full 8-expert problem"
+            self.x, self.w = workloads.moe_inputs(counts, k, n, "bf16", seed=0)
+            self.starts = workloads.offsets_from_counts(counts)
+            self.sample = f"{expr} (worker.py:88-90) on the full 8-expert problem"
             self.work = 2.0 * sum(counts) * k * n
         elif name == "rmsnorm_gemm":
             cfg = workloads.RMSNORM_GEMM
             rows = 256
-            x, w, b = workloads.rmsnorm_gemm_inputs(cfg["m"], cfg["k"], cfg["n"], "bf16", seed=0)
-            self.cx, self.cw, self.cb = (x[:rows].float().numpy(), w.float().numpy(),
-                                         b.float().numpy())
+            x, self.w, self.b = workloads.rmsnorm_gemm_inputs(cfg["m"], cfg["k"], cfg["n"],
+                                                              "bf16", seed=0)
+            self.x = x[:rows].contiguous()
             self.eps = cfg["eps"]
-            self.sample = (f"numpy fp32 RMSNorm of {rows} rows of x, then BLAS fp32 GEMM with B "
-                           f"(K={cfg['k']}, N={cfg['n']})")
+            self.sample = (f"{expr}s, RMSNorm (worker.py:73-74) of {rows} rows of x then GEMM "
+                           f"(worker.py:64) with B (K={cfg['k']}, N={cfg['n']})")
             self.work = 2.0 * rows * cfg["k"] * cfg["n"]
         elif name == "moe_large":
             import torch
 
             cfg = workloads.MOE_LARGE
             g = torch.Generator().manual_seed(0)
-            self.cx = torch.randn(256, cfg["k"], generator=g).bfloat16().float().numpy()
-            self.cw = (0.02 * torch.randn(cfg["k"], cfg["n"], generator=g)).bfloat16().float().numpy()
-            self.sample = "numpy/BLAS fp32 GEMM of 256 tokens x one expert's W[4096, 14336]"
+            self.a = torch.randn(256, cfg["k"], generator=g).bfloat16()
+            self.b = (0.02 * torch.randn(cfg["k"], cfg["n"], generator=g)).bfloat16()
+            self.sample = (f"{expr} of one expert (worker.py:88-90): 256 tokens x "
+                           f"W[{cfg['k']}, {cfg['n']}]")
             self.work = 2.0 * 256 * cfg["k"] * cfg["n"]
         else:
             raise ValueError(name)
 
-    def step(self, pool, threads):
-        from oracle import numerics
+    def step(self):
+        from oracle import reference_cpu as ref
 
         if self.name == "rmsnorm":
-            rows = self.cx.shape[0]
-            chunk = max(1, -(-rows // threads))
-            out = getattr(self, "cout", None)
-            if out is None:
-                import numpy as np
-
-                out = self.cout = np.empty_like(self.cx)
-
-            def work(lo):
-                hi = min(rows, lo + chunk)
-                out[lo:hi] = numerics.rmsnorm_fp32(self.cx[lo:hi], self.cw, self.eps)
-
-            list(pool.map(work, range(0, rows, chunk)))
+            ref.rmsnorm(self.x, self.w, self.eps)
         elif self.name.startswith("gemm") or self.name == "moe_large":
-            numerics.gemm_fp32(self.ca if hasattr(self, "ca") else self.cx,
-                               self.cb if hasattr(self, "cb") else self.cw)
+            ref.gemm(self.a, self.b)
         elif self.name == "moe_small":
-            numerics.grouped_gemm_fp32(self.cx, self.cw, self.cstarts)
+            ref.grouped_gemm(self.x, self.w, self.starts)
         elif self.name == "rmsnorm_gemm":
-            numerics.gemm_fp32(numerics.rmsnorm_fp32(self.cx, self.cw, self.eps), self.cb)
+            ref.rmsnorm_gemm(self.x, self.w, self.b, self.eps)
         return self.work
 
 
 def cpu_measure(name, seconds, min_reps=3):
-    """Time the oracle port of a workload on the host cores for ~``seconds``."""
+    """Time the reference's FP32 CPU path of a workload on the host cores for ~``seconds``."""
+    from oracle import reference_cpu
+
     threads = cpu_threads()
-    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    reference_cpu.configure(threads)
     leg = CpuLeg(name)
-    with ThreadPoolExecutor(threads) as pool:
-        leg.step(pool, threads)  # warm
-        reps, work, t0 = 0, 0.0, time.perf_counter()
-        while reps < min_reps or time.perf_counter() - t0 < seconds:
-            work += leg.step(pool, threads)
-            reps += 1
-        elapsed = time.perf_counter() - t0
+    leg.step()  # warm
+    reps, work, t0 = 0, 0.0, time.perf_counter()
+    while reps < min_reps or time.perf_counter() - t0 < seconds:
+        work += leg.step()
+        reps += 1
+    elapsed = time.perf_counter() - t0
     scale = 1e9 if leg.unit == "GB/s" else 1e12
     return {"value": work / elapsed / scale, "unit": leg.unit, "cores": threads, "kind": "port",
             "sample": f"{leg.sample}; {reps} reps in {elapsed:.1f} s"}
@@ -1179,19 +1169,18 @@ def secondary_names(args):
 
 def reference_entry(name, args, world):
     """One workload of the --impl reference arm: K bounded CPU steps after W untimed ones."""
-    import torch
+    from oracle import reference_cpu
 
-    torch.set_num_threads(cpu_threads())
     threads = cpu_threads()
+    reference_cpu.configure(threads)
     leg = CpuLeg(name)
     times, work = [], 0.0
-    with ThreadPoolExecutor(threads) as pool:
-        for _ in range(args.warmup):
-            leg.step(pool, threads)
-        for _ in range(args.steps):
-            t0 = time.perf_counter()
-            work += leg.step(pool, threads)
-            times.append(time.perf_counter() - t0)
+    for _ in range(args.warmup):
+        leg.step()
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        work += leg.step()
+        times.append(time.perf_counter() - t0)
     total = sum(times)
     scale = 1e9 if leg.unit == "GB/s" else 1e12
     value = work / total / scale
@@ -1206,7 +1195,7 @@ def reference_entry(name, args, world):
 
 
 def run_reference(args):
-    """--impl reference: the reference's FP32 CPU path (oracle port) on the host."""
+    """--impl reference: the reference's FP32 CPU path (its torch expressions) on the host."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0

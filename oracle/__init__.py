@@ -10,6 +10,9 @@ Contents (numpy, fp32 arithmetic, restating the reference's FP32 path):
 * ``numerics``: bf16/fp16 bit conversion, the FP32 references of the three
   kernels (reference ``bo_kernel_tuner/tuner/worker.py:64, 73-74, 88-90``) and
   the correctness gate (``worker.py:108-116``).
+* ``reference_cpu``: the same FP32 formulas as PyTorch expressions on CPU
+  tensors, as the reference's worker writes them; the timed CPU arm of
+  ``bench.py`` runs these (never a checker).
 * ``routing``: MoE expert histogram, offsets (``worker.py:83-86``), stable
   counting-sort permutation and inverse permutation (no reference counterpart;
   ``kernels/moe_grouped_gemm.py:3`` leaves routing outside the operator).

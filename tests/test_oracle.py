@@ -147,3 +147,32 @@ def test_fused_rmsnorm_gemm_restatement_is_exact_algebra():
     ref32 = numerics.rmsnorm_gemm_fp32(x, w, b, eps)
     np.testing.assert_allclose(ref32, chain, rtol=1e-4, atol=1e-5)
     np.testing.assert_allclose(numerics.rmsnorm_row_scale_fp32(x, eps), s, rtol=1e-6)
+
+
+def test_timed_cpu_arm_matches_oracle():
+    """The torch expressions the CPU arm times (oracle.reference_cpu) compute
+    what the numpy oracle computes, on the 16-bit inputs of each kernel."""
+    import torch
+
+    from flashattentionanycard_b200 import workloads
+    from oracle import reference_cpu
+
+    threads = torch.get_num_threads()
+    reference_cpu.configure(2)
+    assert torch.get_num_threads() == 2
+    torch.set_num_threads(threads)
+    a, b = workloads.gemm_inputs(64, 96, 80, "bf16", seed=1)
+    np.testing.assert_allclose(reference_cpu.gemm(a, b).numpy(),
+                               numerics.gemm_fp32(a.float().numpy(), b.float().numpy()),
+                               rtol=1e-5, atol=1e-5)
+    x, w = workloads.rmsnorm_inputs(33, 200, "fp16", seed=2)
+    np.testing.assert_allclose(reference_cpu.rmsnorm(x, w, 1e-6).numpy(),
+                               numerics.rmsnorm_fp32(x.float().numpy(), w.float().numpy(), 1e-6),
+                               rtol=1e-5, atol=1e-5)
+    counts = (0, 5, 17, 0, 9)
+    x, w = workloads.moe_inputs(counts, 48, 40, "bf16", seed=3)
+    starts = workloads.offsets_from_counts(counts)
+    np.testing.assert_allclose(reference_cpu.grouped_gemm(x, w, starts).numpy(),
+                               numerics.grouped_gemm_fp32(x.float().numpy(), w.float().numpy(),
+                                                          starts),
+                               rtol=1e-5, atol=1e-5)
