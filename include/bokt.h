@@ -49,7 +49,7 @@ extern "C" {
 /* status codes */
 #define BOKT_OK 0
 #define BOKT_ERR_INVALID 1     /* bad argument: null pointer, negative size, ... */
-#define BOKT_ERR_UNSUPPORTED 2 /* legal request this build does not implement */
+#define BOKT_ERR_UNSUPPORTED 2 /* legal request the library does not implement */
 #define BOKT_ERR_CONFIG 3      /* launch parameters outside the kernel's domain */
 #define BOKT_ERR_CUDA 4        /* a CUDA runtime/driver call failed */
 #define BOKT_ERR_DEVICE 5      /* a kernel reported a timeout through the device status word */

@@ -2,7 +2,7 @@
 
 Only ``tests/``, ``__graft_entry__.smoke()`` and the ``cpu_baseline`` /
 ``--impl reference`` legs of ``bench.py`` may import this package, and only as
-the checker or as the timed CPU reference.  The product path
+the correctness reference or as the timed CPU reference.  The product path
 (``flashattentionanycard_b200``) never imports it and has no CPU fallback.
 
 Contents (numpy, fp32 arithmetic, restating the reference's FP32 path):
