@@ -70,6 +70,9 @@ struct GemmTcArgs {
 constexpr int kRasterExpert = 1;
 constexpr int kRasterBalanced = 2;
 constexpr int kLowReuseMBlocks = 2;
+// Rows of an expert walked together across its weight column blocks (the
+// grouped tile order); 4096 rows of X are 32 MB at K = 4096.
+constexpr int kExpertRowGroup = 4096;
 
 template <int BN>
 struct GemmTcShape {
@@ -346,10 +349,19 @@ __device__ __forceinline__ TileCoord grouped_tile(int t, const GroupedSchedule& 
   const int rel = u - g.pre[lo];
   const int count = g.pcount[lo];
   const int mblocks = (count + tile_rows - 1) / tile_rows;
-  // M fastest inside an expert: all row blocks of one weight column block run
-  // together, so W[e][:, n-block] is fetched from HBM once and reused from L2.
-  const int mb = rel % mblocks;
-  const int nb = rel / mblocks;
+  // M fastest inside a group of row blocks: all row blocks of the group run
+  // together on one weight column block, so W[e][:, n-block] is fetched from
+  // HBM once per group and reused from L2.  Groups span kExpertRowGroup rows,
+  // so that the group's X rows stay in L2 while it walks the expert's column
+  // blocks; an expert with more rows (a hot expert) is split into groups.
+  const int gsize = kExpertRowGroup / tile_rows;  // row blocks per group
+  const int per_group = gsize * nn;
+  const int grp = rel / per_group;
+  const int gfirst = grp * gsize;
+  const int gm = min(mblocks - gfirst, gsize);
+  const int local = rel - grp * per_group;
+  const int mb = gfirst + local % gm;
+  const int nb = local / gm;
   TileCoord c;
   c.a_row = g.pstart[lo] + mb * tile_rows;
   c.n0 = nb * bn;
