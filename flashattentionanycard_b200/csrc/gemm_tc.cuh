@@ -140,13 +140,20 @@ __device__ __forceinline__ void epilogue_store_tile(uint32_t taddr, uint8_t* sta
     __syncwarp();
     const int cc = lane & 7;
     const int col = n0 + c + cc * 8;
+    // All eight staged segments and row pointers are read before the first
+    // global store: a shared-memory load after a store through a generic
+    // pointer would otherwise wait for that store, one round trip per row.
+    uint4 d[8];
+    OutT* rp[8];
 #pragma unroll
     for (int it = 0; it < 8; ++it) {
       const int r = it * 4 + (lane >> 3);
-      const uint4 d = *reinterpret_cast<const uint4*>(stage + r * 128 + ((cc ^ (r & 7)) << 4));
-      OutT* rp = rowptr[r];
-      if (rp != nullptr && col < N) *reinterpret_cast<uint4*>(rp + c + cc * 8) = d;
+      d[it] = *reinterpret_cast<const uint4*>(stage + r * 128 + ((cc ^ (r & 7)) << 4));
+      rp[it] = rowptr[r];
     }
+#pragma unroll
+    for (int it = 0; it < 8; ++it)
+      if (rp[it] != nullptr && col < N) *reinterpret_cast<uint4*>(rp[it] + c + cc * 8) = d[it];
     __syncwarp();
   }
 }
